@@ -1,0 +1,26 @@
+"""CPU oracle for the FP8 quantize / scaled-BMM path.
+
+TEST INFRASTRUCTURE ONLY.  Nothing in ``practice_cuda_b200`` imports this
+package: it is the checker used by ``tests/``, ``__graft_entry__.smoke()`` and
+the ``cpu_baseline`` / ``--impl reference`` legs of ``bench.py``.  The product
+path runs the CUDA library and fails loudly when it is missing.
+
+Parity pin: the restatement is checked against vectors produced by the
+reference's own torch functions (``tests/golden/make_golden.py``) -- the
+per-channel torch quantizer, the legacy per-tensor test reference, and the
+registry's ``QuantResult.dequantize``.
+"""
+
+from .quant import (  # noqa: F401
+    FP8_MAX,
+    per_block_quant,
+    per_channel_quant,
+    per_tensor_quant,
+    legacy_per_tensor_quant,
+    dequantize,
+)
+from .gemm import (  # noqa: F401
+    scaled_bmm_dequant_reference,
+    scaled_bmm_promoted_reference,
+    legacy_bmm_reference,
+)

@@ -1,0 +1,446 @@
+// Scaled FP8 batched GEMM for sm_100a: TMA -> shared memory ring -> tcgen05.mma
+// (kind::f8f6f4, fp32 accumulators in TMEM) -> epilogue warps that promote
+// every K quant group with its fp32 scales into register accumulators.
+//
+// CTA = 12 warps, persistent over output tiles (one CTA per SM):
+//   warp 0      TMA producer (one elected lane), no multicast
+//   warp 1      TMEM allocator + MMA issuer (one elected lane)
+//   warps 2-3   idle
+//   warps 4-11  epilogue: two warpgroups; warpgroup h owns tile columns
+//               [h*BN/2, (h+1)*BN/2), warp (w % 4) owns TMEM lanes / rows
+//               [32*(w%4), 32*(w%4)+32).
+// TMEM holds two accumulator buffers of BN fp32 columns each, so the MMA of
+// K-group g+1 runs while the epilogue promotes group g.
+#pragma once
+
+#include "common.cuh"
+
+namespace pcb {
+namespace gemm {
+
+constexpr int BM = 128;           // rows per tile (UMMA M)
+constexpr int BK = 128;           // K elements per pipeline stage = one 128-byte swizzle atom
+constexpr int UMMA_K = 32;        // K per tcgen05.mma for 8-bit inputs
+constexpr int kThreads = 384;
+constexpr int kEpiWarp0 = 4;
+constexpr int kEpiThreads = 256;
+
+struct Params {
+  int batch, m, n, k;
+  int m_blocks, n_blocks, num_tiles;
+  int k_stages;          // ceil(k / BK)
+  int stages_per_group;  // qbk / BK (or k_stages for a single group)
+  int num_groups;        // ceil(k_stages / stages_per_group)
+  // scale_a[b*ssab + (m/qbm)*ssam + g*ssak]; scale_b[b*ssbb + g*ssbk + (n/qbn)*ssbn]
+  const float* sa;
+  long long ssab, ssam, ssak;
+  int qbm;
+  const float* sb;
+  long long ssbb, ssbk, ssbn;
+  int qbn;
+  int col_uniform;  // sb constant over each warpgroup's column half
+  // output / bias
+  void* c;
+  long long scb, scm;
+  int c_dtype;
+  int c_vec;  // 16-byte vector stores allowed
+  const void* bias;
+  long long sbib, sbim, sbin;
+  int bias_dtype;
+  int activation;
+  int inject_error;
+};
+
+// ---------------------------------------------------------------------------
+// PTX wrappers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1,
+                                            int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+      "[%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void umma_f8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on `bar` once every previously issued tcgen05.mma of this thread completes.
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
+// 32 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// UMMA shared-memory descriptor for a 128-byte-swizzled tile.
+//   K-major : rows of 128 bytes (BK fp8), 8-row atoms 1024 B apart (SBO).
+//   MN-major: 128-element MN slabs, K rows 128 B apart; 8-K-row atoms 1024 B
+//             apart (SBO); consecutive 128-wide MN slabs `lbo` bytes apart.
+__device__ __forceinline__ uint64_t make_sw128_desc(uint32_t saddr, uint32_t lbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)(1024u >> 4) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version for tcgen05
+  d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: fp32 accumulate, fp8 A/B, M=128, N=BN.
+__host__ __device__ constexpr uint32_t make_idesc(int bn, int ab_fmt, int a_mn, int b_mn) {
+  return (1u << 4) | ((uint32_t)ab_fmt << 7) | ((uint32_t)ab_fmt << 10) | ((uint32_t)a_mn << 15) |
+         ((uint32_t)b_mn << 16) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+template <int BN>
+struct Smem {
+  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int A_BYTES = BM * BK;  // 16 KB
+  static constexpr int B_BYTES = BN * BK;  // 32 / 16 KB
+  static constexpr int EPI_COLS = BN / 2;
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
+  static constexpr int OFF_COLSCALE = OFF_B + STAGES * B_BYTES;           // 8 warps x EPI_COLS floats
+  static constexpr int OFF_BAR = OFF_COLSCALE + 8 * EPI_COLS * 4;
+  static constexpr int NUM_BARS = 2 * STAGES + 4;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;                  // tmem addr, abort flag
+  static constexpr int BYTES = OFF_MISC + 16;
+  static constexpr int ALLOC = BYTES + 1024;                              // slack for 1 KB alignment
+};
+
+__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.7071067811865475f)); }
+
+__device__ __forceinline__ float load_bias(const void* p, int dt, long long off) {
+  if (dt == PCB_DTYPE_F32) return __ldg(static_cast<const float*>(p) + off);
+  if (dt == PCB_DTYPE_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[off]);
+  return __half2float(static_cast<const __half*>(p)[off]);
+}
+
+template <int BN, bool A_MN, bool B_MN, int AB_FMT>
+__global__ void __launch_bounds__(kThreads, 1)
+    bmm_scaled_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                      const Params p) {
+  using S = Smem<BN>;
+  constexpr int STAGES = S::STAGES;
+  constexpr int EPI_COLS = S::EPI_COLS;
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+  constexpr uint32_t IDESC = make_idesc(BN, AB_FMT, A_MN ? 1 : 0, B_MN ? 1 : 0);
+  constexpr uint32_t STAGE_TX = S::A_BYTES + S::B_BYTES;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t s_base = smem_u32(smem);
+  const uint32_t bar_full = s_base + S::OFF_BAR;                  // [STAGES]
+  const uint32_t bar_empty = bar_full + 8 * STAGES;               // [STAGES]
+  const uint32_t bar_tfull = bar_empty + 8 * STAGES;              // [2]
+  const uint32_t bar_tempty = bar_tfull + 16;                     // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar_tfull + 8 * i, 1);
+      mbar_init(bar_tempty + 8 * i, 8);  // one arrive per epilogue warp
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_b);
+  }
+  if (warp == 1) tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+
+  if (p.inject_error && blockIdx.x == 0 && threadIdx.x == 0) report_error(p.inject_error, SITE_GEMM_INJECTED);
+
+  const int tiles_per_batch = p.m_blocks * p.n_blocks;
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        const int b = tile / tiles_per_batch;
+        const int rem = tile - b * tiles_per_batch;
+        const int mb = rem / p.n_blocks;
+        const int nb = rem - mb * p.n_blocks;
+        for (int ks = 0; ks < p.k_stages; ++ks) {
+          if (!mbar_wait_bounded(bar_empty + 8 * stage, phase ^ 1, abort_flag, SITE_GEMM_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = bar_full + 8 * stage;
+          mbar_arrive_expect_tx(fb, STAGE_TX);
+          const uint32_t sa_dst = s_base + S::OFF_A + stage * S::A_BYTES;
+          const uint32_t sb_dst = s_base + S::OFF_B + stage * S::B_BYTES;
+          if constexpr (A_MN) {
+            tma_load_3d(sa_dst, &tmap_a, fb, mb * BM, ks * BK, b);
+          } else {
+            tma_load_3d(sa_dst, &tmap_a, fb, ks * BK, mb * BM, b);
+          }
+          if constexpr (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 128; ++j) tma_load_3d(sb_dst + j * 128 * BK, &tmap_b, fb, nb * BN + j * 128, ks * BK, b);
+          } else {
+            tma_load_3d(sb_dst, &tmap_b, fb, ks * BK, nb * BN, b);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // Let the copies already issued land before the CTA can exit.
+        for (int s = 0; s < STAGES; ++s) mbar_wait_bounded(bar_full + 8 * s, 0, abort_flag, SITE_GEMM_PRODUCER);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------- MMA issuer -------------------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t acc_cnt = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        for (int g = 0; g < p.num_groups && ok; ++g) {
+          const uint32_t abuf = acc_cnt & 1;
+          const uint32_t aphase = (acc_cnt >> 1) & 1;
+          if (!mbar_wait_bounded(bar_tempty + 8 * abuf, aphase ^ 1, abort_flag, SITE_GEMM_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + abuf * BN;
+          const int ks0 = g * p.stages_per_group;
+          const int ks1 = min(p.k_stages, ks0 + p.stages_per_group);
+          for (int ks = ks0; ks < ks1; ++ks) {
+            if (!mbar_wait_bounded(bar_full + 8 * stage, phase, abort_flag, SITE_GEMM_MMA)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t sa_addr = s_base + S::OFF_A + stage * S::A_BYTES;
+            const uint32_t sb_addr = s_base + S::OFF_B + stage * S::B_BYTES;
+            const uint64_t adesc0 = make_sw128_desc(sa_addr, A_MN ? (uint32_t)(128 * BK) : 16u);
+            const uint64_t bdesc0 = make_sw128_desc(sb_addr, B_MN ? (uint32_t)(128 * BK) : 16u);
+#pragma unroll
+            for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+              // K advance inside the stage: 32 bytes along a K-major row, or
+              // 32 rows of 128 bytes for an MN-major tile (encoded >> 4).
+              const uint64_t a_off = A_MN ? (uint64_t)(kk * UMMA_K * 128 >> 4) : (uint64_t)(kk * UMMA_K >> 4);
+              const uint64_t b_off = B_MN ? (uint64_t)(kk * UMMA_K * 128 >> 4) : (uint64_t)(kk * UMMA_K >> 4);
+              umma_f8(d_tmem, adesc0 + a_off, bdesc0 + b_off, IDESC, (ks > ks0 || kk > 0) ? 1u : 0u);
+            }
+            umma_commit(bar_empty + 8 * stage);  // smem stage free once these MMAs retire
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+          if (!ok) break;
+          umma_commit(bar_tfull + 8 * abuf);  // accumulator of group g ready
+          ++acc_cnt;
+        }
+      }
+    }
+  } else if (warp >= kEpiWarp0) {
+    // -------------------------------- epilogue --------------------------------
+    const int ew = warp - kEpiWarp0;        // 0..7
+    const int quarter = warp & 3;           // TMEM lane quarter
+    const int half = ew >> 2;               // column half
+    const int row_in_tile = quarter * 32 + lane;
+    float* colscale = reinterpret_cast<float*>(smem + S::OFF_COLSCALE) + ew * EPI_COLS;
+    uint32_t acc_cnt = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      const int b = tile / tiles_per_batch;
+      const int rem = tile - b * tiles_per_batch;
+      const int mb = rem / p.n_blocks;
+      const int nb = rem - mb * p.n_blocks;
+      const int row = mb * BM + row_in_tile;
+      const int col0 = nb * BN + half * EPI_COLS;
+      const bool row_ok = row < p.m;
+      const float* sa_row = p.sa ? p.sa + (long long)b * p.ssab + (long long)(row / p.qbm) * p.ssam : nullptr;
+      const float* sb_b = p.sb ? p.sb + (long long)b * p.ssbb : nullptr;
+
+      float acc[EPI_COLS];
+#pragma unroll
+      for (int i = 0; i < EPI_COLS; ++i) acc[i] = 0.f;
+
+      for (int g = 0; g < p.num_groups; ++g) {
+        const uint32_t abuf = acc_cnt & 1;
+        const uint32_t aphase = (acc_cnt >> 1) & 1;
+        // Scales for this group (loaded before the wait to hide latency).
+        const float s_row = (sa_row && row_ok) ? __ldg(sa_row + (long long)g * p.ssak) : 1.f;
+        float s_col = 1.f;
+        if (p.col_uniform) {
+          if (sb_b && col0 < p.n) s_col = __ldg(sb_b + (long long)g * p.ssbk + (long long)(col0 / p.qbn) * p.ssbn);
+        } else {
+          __syncwarp();
+#pragma unroll
+          for (int i = lane; i < EPI_COLS; i += 32) {
+            const int c = col0 + i;
+            colscale[i] = (sb_b && c < p.n) ? __ldg(sb_b + (long long)g * p.ssbk + (long long)(c / p.qbn) * p.ssbn) : 1.f;
+          }
+          __syncwarp();
+        }
+        if (!mbar_wait_bounded(bar_tfull + 8 * abuf, aphase, abort_flag, SITE_GEMM_EPILOGUE)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN + half * EPI_COLS;
+#pragma unroll
+        for (int j = 0; j < EPI_COLS / 32; ++j) {
+          float v[32];
+          tmem_ld32(taddr + j * 32, v);
+          if (p.col_uniform) {
+            const float s = s_row * s_col;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc[j * 32 + i] = fmaf(v[i], s, acc[j * 32 + i]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc[j * 32 + i] = fmaf(v[i], s_row * colscale[j * 32 + i], acc[j * 32 + i]);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_tempty + 8 * abuf);
+        ++acc_cnt;
+      }
+      if (!ok) break;
+
+      // Bias, activation, cast, store.
+      if (row_ok) {
+        const long long crow = (long long)b * p.scb + (long long)row * p.scm;
+        if (p.bias) {
+#pragma unroll
+          for (int i = 0; i < EPI_COLS; ++i) {
+            const int c = col0 + i;
+            if (c < p.n)
+              acc[i] += load_bias(p.bias, p.bias_dtype, (long long)b * p.sbib + (long long)row * p.sbim + (long long)c * p.sbin);
+          }
+        }
+        if (p.activation == PCB_ACT_GELU) {
+#pragma unroll
+          for (int i = 0; i < EPI_COLS; ++i) acc[i] = gelu_erf(acc[i]);
+        }
+        const bool full = p.c_vec && (col0 + EPI_COLS <= p.n);
+        if (p.c_dtype == PCB_DTYPE_BF16 || p.c_dtype == PCB_DTYPE_F16) {
+          uint16_t* out = static_cast<uint16_t*>(p.c) + crow + col0;
+          if (full) {
+#pragma unroll
+            for (int i = 0; i < EPI_COLS; i += 8) {
+              uint4 w;
+              uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                if (p.c_dtype == PCB_DTYPE_BF16) {
+                  __nv_bfloat162 h = __floats2bfloat162_rn(acc[i + 2 * q], acc[i + 2 * q + 1]);
+                  wp[q] = *reinterpret_cast<uint32_t*>(&h);
+                } else {
+                  __half2 h = __floats2half2_rn(acc[i + 2 * q], acc[i + 2 * q + 1]);
+                  wp[q] = *reinterpret_cast<uint32_t*>(&h);
+                }
+              }
+              *reinterpret_cast<uint4*>(out + i) = w;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < EPI_COLS; ++i) {
+              if (col0 + i < p.n) {
+                if (p.c_dtype == PCB_DTYPE_BF16) {
+                  __nv_bfloat16 h = __float2bfloat16_rn(acc[i]);
+                  out[i] = *reinterpret_cast<uint16_t*>(&h);
+                } else {
+                  __half h = __float2half_rn(acc[i]);
+                  out[i] = *reinterpret_cast<uint16_t*>(&h);
+                }
+              }
+            }
+          }
+        } else if (p.c_dtype == PCB_DTYPE_F32) {
+          float* out = static_cast<float*>(p.c) + crow + col0;
+          if (full) {
+#pragma unroll
+            for (int i = 0; i < EPI_COLS; i += 4)
+              *reinterpret_cast<float4*>(out + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < EPI_COLS; ++i)
+              if (col0 + i < p.n) out[i] = acc[i];
+          }
+        } else {
+          uint8_t* out = static_cast<uint8_t*>(p.c) + crow + col0;
+#pragma unroll
+          for (int i = 0; i < EPI_COLS; ++i) {
+            if (col0 + i < p.n)
+              out[i] = (p.c_dtype == PCB_DTYPE_E4M3) ? cvt1_fp8<PCB_DTYPE_E4M3>(acc[i]) : cvt1_fp8<PCB_DTYPE_E5M2>(acc[i]);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
+}  // namespace gemm
+}  // namespace pcb

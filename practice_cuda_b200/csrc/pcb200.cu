@@ -1,0 +1,475 @@
+// libpcb200: the C ABI (include/pcb200.h) over the sm_100a kernels.
+// One translation unit so the device error word is a single symbol.
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+#include "gemm_sm100.cuh"
+#include "quant_kernels.cuh"
+
+using namespace pcb;
+
+namespace {
+
+thread_local std::string g_last_error;
+std::atomic<int> g_inject_error{0};
+
+int fail(int status, const char* what) {
+  g_last_error = what;
+  return status;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    g_last_error = std::string(what) + ": " + cudaGetErrorString(e);
+    return PCB_ERR_LAUNCH;
+  }
+  return PCB_OK;
+}
+
+struct DeviceInfo {
+  int sm_count = 0;
+  int major = 0;
+};
+
+DeviceInfo device_info() {
+  static std::mutex mu;
+  static DeviceInfo cache[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev].sm_count == 0) {
+    cudaDeviceGetAttribute(&cache[dev].sm_count, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&cache[dev].major, cudaDevAttrComputeCapabilityMajor, dev);
+  }
+  return cache[dev];
+}
+
+bool aligned(const void* p, int64_t a) { return (reinterpret_cast<uintptr_t>(p) % (uintptr_t)a) == 0; }
+
+int elem_size(int dt) {
+  switch (dt) {
+    case PCB_DTYPE_F32: return 4;
+    case PCB_DTYPE_F16:
+    case PCB_DTYPE_BF16: return 2;
+    case PCB_DTYPE_E4M3:
+    case PCB_DTYPE_E5M2: return 1;
+    default: return 0;
+  }
+}
+
+bool is_float_in(int dt) { return dt == PCB_DTYPE_F32 || dt == PCB_DTYPE_F16 || dt == PCB_DTYPE_BF16; }
+bool is_fp8(int dt) { return dt == PCB_DTYPE_E4M3 || dt == PCB_DTYPE_E5M2; }
+
+// Dispatch a functor over (input dtype, fp8 output dtype) as compile-time ints.
+template <typename F>
+int dispatch_xy(int xt, int yt, F&& f) {
+  auto with_y = [&](auto xc) -> int {
+    if (yt == PCB_DTYPE_E4M3) return f(xc, std::integral_constant<int, PCB_DTYPE_E4M3>{});
+    if (yt == PCB_DTYPE_E5M2) return f(xc, std::integral_constant<int, PCB_DTYPE_E5M2>{});
+    return fail(PCB_ERR_INVALID, "output dtype must be E4M3 or E5M2");
+  };
+  if (xt == PCB_DTYPE_F32) return with_y(std::integral_constant<int, PCB_DTYPE_F32>{});
+  if (xt == PCB_DTYPE_F16) return with_y(std::integral_constant<int, PCB_DTYPE_F16>{});
+  if (xt == PCB_DTYPE_BF16) return with_y(std::integral_constant<int, PCB_DTYPE_BF16>{});
+  return fail(PCB_ERR_INVALID, "input dtype must be F32, F16 or BF16");
+}
+
+// ---------------------------------------------------------------------------
+// Grouped quantization (per-block and per-channel rows share this driver).
+// ---------------------------------------------------------------------------
+int launch_groups(const void* x, int xt, int64_t batch, int64_t m, int64_t n, int64_t sxb, int64_t sxm, int64_t sxn,
+                  void* y, int yt, int64_t syb, int64_t sym, int64_t syn, float* scale, int64_t ssb, int64_t ssm,
+                  int64_t ssn, int64_t gm, int64_t gn, int mode, float eps, cudaStream_t stream) {
+  const int es = elem_size(xt);
+  const int vec = 16 / es;
+  const int64_t groups_m = (m + gm - 1) / gm, groups_n = (n + gn - 1) / gn;
+  const int64_t num_groups = batch * groups_m * groups_n;
+  if (num_groups == 0) return PCB_OK;
+  const DeviceInfo di = device_info();
+  const bool vec_ok = sxn == 1 && syn == 1 && n % vec == 0 && gn % vec == 0 && aligned(x, 16) &&
+                      (sxm * es) % 16 == 0 && (batch == 1 || (sxb * es) % 16 == 0) && aligned(y, vec) &&
+                      sym % vec == 0 && (batch == 1 || syb % vec == 0);
+  if (vec_ok) {
+    quant::GroupArgs a{x, sxb, sxm, y, syb, sym, scale, ssb, ssm, ssn, batch, m, n, gm, gn, groups_m, groups_n,
+                       num_groups, eps};
+    const int64_t nch = gm * gn / vec;
+    return dispatch_xy(xt, yt, [&](auto xc, auto yc) -> int {
+      constexpr int XT = decltype(xc)::value;
+      constexpr int YT = decltype(yc)::value;
+      auto go = [&](auto kernel, int team) -> int {
+        const int64_t teams_per_cta = quant::kThreads / team;
+        int64_t grid = (num_groups + teams_per_cta - 1) / teams_per_cta;
+        grid = std::min<int64_t>(grid, (int64_t)di.sm_count * 8);
+        kernel<<<(unsigned)grid, quant::kThreads, 0, stream>>>(a);
+        return check_launch("quant_groups_kernel");
+      };
+      if (mode == quant::kDeqReciprocal) {
+        if (nch <= 16) return go(quant::quant_groups_kernel<XT, YT, 8, 2, quant::kDeqReciprocal>, 8);
+        if (nch <= 32) return go(quant::quant_groups_kernel<XT, YT, 16, 2, quant::kDeqReciprocal>, 16);
+        if (nch <= 128) return go(quant::quant_groups_kernel<XT, YT, 32, 4, quant::kDeqReciprocal>, 32);
+        return go(quant::quant_groups_kernel<XT, YT, 256, 8, quant::kDeqReciprocal>, 256);
+      } else {
+        if (nch <= 16) return go(quant::quant_groups_kernel<XT, YT, 8, 2, quant::kDeqDivide>, 8);
+        if (nch <= 32) return go(quant::quant_groups_kernel<XT, YT, 16, 2, quant::kDeqDivide>, 16);
+        if (nch <= 128) return go(quant::quant_groups_kernel<XT, YT, 32, 4, quant::kDeqDivide>, 32);
+        return go(quant::quant_groups_kernel<XT, YT, 256, 8, quant::kDeqDivide>, 256);
+      }
+    });
+  }
+  quant::GenericArgs a{x, sxb, sxm, sxn, y, syb, sym, syn, scale, ssb, ssm, ssn, batch, m, n, gm, gn,
+                       groups_m, groups_n, num_groups, eps};
+  return dispatch_xy(xt, yt, [&](auto xc, auto yc) -> int {
+    constexpr int XT = decltype(xc)::value;
+    constexpr int YT = decltype(yc)::value;
+    const int64_t grid = std::min<int64_t>(num_groups, (int64_t)di.sm_count * 8);
+    if (mode == quant::kDeqReciprocal)
+      quant::quant_groups_generic_kernel<XT, YT, quant::kDeqReciprocal><<<(unsigned)grid, quant::kThreads, 0, stream>>>(a);
+    else
+      quant::quant_groups_generic_kernel<XT, YT, quant::kDeqDivide><<<(unsigned)grid, quant::kThreads, 0, stream>>>(a);
+    return check_launch("quant_groups_generic_kernel");
+  });
+}
+
+// ---------------------------------------------------------------------------
+// TMA descriptors (driver entry point fetched through the runtime, so the
+// library does not link libcuda directly).
+// ---------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 3-D uint8 map (inner, outer, batch) with a 128-byte swizzled box (128, box_outer, 1).
+bool make_map_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t batch,
+                 uint64_t outer_stride, uint64_t batch_stride, uint32_t box_outer) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {inner, outer, batch};
+  if (batch <= 1) {
+    batch_stride = ((outer * outer_stride + 15) / 16) * 16;
+    if (batch_stride == 0) batch_stride = 16;
+  }
+  cuuint64_t strides[2] = {outer_stride, batch_stride};
+  cuuint32_t box[3] = {128, box_outer, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <typename K>
+void ensure_smem_attr(K kernel, int bytes) {
+  // cudaFuncSetAttribute is per function and device; calling it again is cheap
+  // and keeps this stateless across devices and threads.
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+template <int BN, bool A_MN, bool B_MN, int FMT>
+int launch_bmm(const CUtensorMap& ta, const CUtensorMap& tb, const gemm::Params& p, int sm_count,
+               cudaStream_t stream) {
+  using S = gemm::Smem<BN>;
+  auto kernel = gemm::bmm_scaled_kernel<BN, A_MN, B_MN, FMT>;
+  ensure_smem_attr(kernel, S::ALLOC);
+  const int grid = std::min(p.num_tiles, sm_count);
+  kernel<<<grid, gemm::kThreads, S::ALLOC, stream>>>(ta, tb, p);
+  return check_launch("bmm_scaled_kernel");
+}
+
+template <int BN>
+int dispatch_bmm_layout(bool a_mn, bool b_mn, int fmt, const CUtensorMap& ta, const CUtensorMap& tb,
+                        const gemm::Params& p, int sm, cudaStream_t s) {
+  if (fmt == 0) {
+    if (!a_mn && !b_mn) return launch_bmm<BN, false, false, 0>(ta, tb, p, sm, s);
+    if (!a_mn && b_mn) return launch_bmm<BN, false, true, 0>(ta, tb, p, sm, s);
+    if (a_mn && !b_mn) return launch_bmm<BN, true, false, 0>(ta, tb, p, sm, s);
+    return launch_bmm<BN, true, true, 0>(ta, tb, p, sm, s);
+  }
+  if (!a_mn && !b_mn) return launch_bmm<BN, false, false, 1>(ta, tb, p, sm, s);
+  if (!a_mn && b_mn) return launch_bmm<BN, false, true, 1>(ta, tb, p, sm, s);
+  if (a_mn && !b_mn) return launch_bmm<BN, true, false, 1>(ta, tb, p, sm, s);
+  return launch_bmm<BN, true, true, 1>(ta, tb, p, sm, s);
+}
+
+}  // namespace
+
+extern "C" {
+
+int pcb_version(void) { return PCB200_ABI_VERSION; }
+
+const char* pcb_status_name(int status) {
+  switch (status) {
+    case PCB_OK: return "PCB_OK";
+    case PCB_ERR_INVALID: return "PCB_ERR_INVALID";
+    case PCB_ERR_UNSUPPORTED: return "PCB_ERR_UNSUPPORTED";
+    case PCB_ERR_LAYOUT: return "PCB_ERR_LAYOUT";
+    case PCB_ERR_LAUNCH: return "PCB_ERR_LAUNCH";
+    case PCB_ERR_DEVICE: return "PCB_ERR_DEVICE";
+    case PCB_ERR_TIMEOUT: return "PCB_ERR_TIMEOUT";
+    default: return "PCB_ERR_UNKNOWN";
+  }
+}
+
+const char* pcb_last_error_text(void) { return g_last_error.c_str(); }
+
+int pcb_get_device_error(int* code, int* site, int* info) {
+  unsigned int h[3] = {0, 0, 0};
+  if (cudaDeviceSynchronize() != cudaSuccess) return check_launch("pcb_get_device_error sync");
+  if (cudaMemcpyFromSymbol(h, pcb::g_device_error, sizeof(h)) != cudaSuccess)
+    return check_launch("pcb_get_device_error read");
+  const unsigned int zero[3] = {0, 0, 0};
+  if (cudaMemcpyToSymbol(pcb::g_device_error, zero, sizeof(zero)) != cudaSuccess)
+    return check_launch("pcb_get_device_error clear");
+  if (code) *code = (int)h[0];
+  if (site) *site = (int)h[1];
+  if (info) *info = (int)h[2];
+  return PCB_OK;
+}
+
+int pcb_debug_inject_error(int code) {
+  g_inject_error.store(code);
+  return PCB_OK;
+}
+
+int pcb_quant_per_block(const void* x, int x_dtype, int64_t batch, int64_t m, int64_t n, int64_t sxb, int64_t sxm,
+                        int64_t sxn, void* y, int y_dtype, int64_t syb, int64_t sym, int64_t syn, float* scale,
+                        int64_t ssb, int64_t ssm, int64_t ssn, int64_t block_m, int64_t block_n, float eps,
+                        void* stream) {
+  if (batch < 0 || m < 0 || n < 0) return fail(PCB_ERR_INVALID, "negative size");
+  if (block_m <= 0 || block_n <= 0) return fail(PCB_ERR_INVALID, "block sizes must be positive");
+  if (batch * m * n == 0) return PCB_OK;
+  if (!x || !y || !scale) return fail(PCB_ERR_INVALID, "null pointer");
+  if (!is_float_in(x_dtype) || !is_fp8(y_dtype)) return fail(PCB_ERR_INVALID, "bad dtype");
+  return launch_groups(x, x_dtype, batch, m, n, sxb, sxm, sxn, y, y_dtype, syb, sym, syn, scale, ssb, ssm, ssn,
+                       block_m, block_n, quant::kDeqReciprocal, eps, (cudaStream_t)stream);
+}
+
+int pcb_quant_per_channel(const void* x, int x_dtype, int64_t batch, int64_t m, int64_t n, int64_t sxb, int64_t sxm,
+                          int64_t sxn, void* y, int y_dtype, int64_t syb, int64_t sym, int64_t syn, float* scale,
+                          int64_t ssb, int64_t ssc, int channel_axis, float eps, void* stream) {
+  if (batch < 0 || m < 0 || n < 0) return fail(PCB_ERR_INVALID, "negative size");
+  if (channel_axis != -1 && channel_axis != -2) return fail(PCB_ERR_INVALID, "channel_axis must be -1 or -2");
+  if (batch * m * n == 0) return PCB_OK;
+  if (!x || !y || !scale) return fail(PCB_ERR_INVALID, "null pointer");
+  if (!is_float_in(x_dtype) || !is_fp8(y_dtype)) return fail(PCB_ERR_INVALID, "bad dtype");
+  cudaStream_t s = (cudaStream_t)stream;
+  if (channel_axis == -2) {
+    // One group per row: (1 x n), scale index (b, row).
+    return launch_groups(x, x_dtype, batch, m, n, sxb, sxm, sxn, y, y_dtype, syb, sym, syn, scale, ssb, ssc, 0, 1, n,
+                         quant::kDeqDivide, eps, s);
+  }
+  // One scale per column.
+  if (sxm == 1 && sym == 1 && !(sxn == 1 && m > 1)) {
+    // Column-contiguous storage: a column is a contiguous run -> rows of x^T.
+    return launch_groups(x, x_dtype, batch, n, m, sxb, sxn, sxm, y, y_dtype, syb, syn, sym, scale, ssb, ssc, 0, 1, m,
+                         quant::kDeqDivide, eps, s);
+  }
+  const int es = elem_size(x_dtype);
+  const int vec = 16 / es;
+  const bool vec_ok = sxn == 1 && syn == 1 && n % vec == 0 && aligned(x, 16) && (sxm * es) % 16 == 0 &&
+                      (batch == 1 || (sxb * es) % 16 == 0) && aligned(y, vec) && sym % vec == 0 &&
+                      (batch == 1 || syb % vec == 0);
+  if (!vec_ok) {
+    return launch_groups(x, x_dtype, batch, m, n, sxb, sxm, sxn, y, y_dtype, syb, sym, syn, scale, ssb, 0, ssc, m, 1,
+                         quant::kDeqDivide, eps, s);
+  }
+  const int sw = 8 * vec;
+  const int cl = (int)std::min<int64_t>(8, std::max<int64_t>(1, (m + 255) / 256));
+  quant::ColArgs a{x, sxb, sxm, y, syb, sym, scale, ssb, ssc, m, n, (int)((m + cl - 1) / cl), eps};
+  return dispatch_xy(x_dtype, y_dtype, [&](auto xc, auto yc) -> int {
+    constexpr int XT = decltype(xc)::value;
+    constexpr int YT = decltype(yc)::value;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((n + sw - 1) / sw), (unsigned)cl, (unsigned)batch);
+    cfg.blockDim = dim3(quant::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = (unsigned)cl;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, quant::quant_cols_cluster_kernel<XT, YT>, a);
+    return check_launch("quant_cols_cluster_kernel");
+  });
+}
+
+int64_t pcb_quant_per_tensor_workspace_floats(void) { return quant::kPerTensorMaxPartials; }
+
+int pcb_quant_per_tensor(const void* x, int x_dtype, int64_t batch, int64_t m, int64_t n, int64_t sxb, int64_t sxm,
+                         int64_t sxn, void* y, int y_dtype, int64_t syb, int64_t sym, int64_t syn, float* quant_scale,
+                         float* dequant_scale, int scale_dtype, float fp8_max, float eps, float* workspace,
+                         void* stream) {
+  if (batch < 0 || m < 0 || n < 0) return fail(PCB_ERR_INVALID, "negative size");
+  if (!x || !y || !workspace) return fail(PCB_ERR_INVALID, "null pointer");
+  if (!is_float_in(x_dtype) || !is_fp8(y_dtype) || !is_float_in(scale_dtype)) return fail(PCB_ERR_INVALID, "bad dtype");
+  cudaStream_t s = (cudaStream_t)stream;
+  const DeviceInfo di = device_info();
+  const int es = elem_size(x_dtype);
+  const int vec = 16 / es;
+  const bool vec_ok = sxn == 1 && syn == 1 && n % vec == 0 && aligned(x, 16) && (sxm * es) % 16 == 0 &&
+                      (batch == 1 || (sxb * es) % 16 == 0) && aligned(y, vec) && sym % vec == 0 &&
+                      (batch == 1 || syb % vec == 0);
+  const int64_t total = batch * m * n;
+  const int64_t per_cta = (int64_t)quant::kThreads * (vec_ok ? vec : 1);
+  int amax_grid = (int)std::min<int64_t>(std::max<int64_t>(1, (total + per_cta - 1) / per_cta),
+                                         std::min<int64_t>(quant::kPerTensorMaxPartials, (int64_t)di.sm_count * 4));
+  quant::TensorArgs a{x, sxb, sxm, sxn, y, syb, sym, syn, batch, m, n, vec_ok, workspace, amax_grid,
+                      quant_scale, dequant_scale, scale_dtype, fp8_max, eps};
+  return dispatch_xy(x_dtype, y_dtype, [&](auto xc, auto yc) -> int {
+    constexpr int XT = decltype(xc)::value;
+    constexpr int YT = decltype(yc)::value;
+    quant::tensor_amax_kernel<XT><<<amax_grid, quant::kThreads, 0, s>>>(a);
+    int st = check_launch("tensor_amax_kernel");
+    if (st != PCB_OK) return st;
+    const int cast_grid = (int)std::min<int64_t>(std::max<int64_t>(1, (total + per_cta - 1) / per_cta),
+                                                 (int64_t)di.sm_count * 8);
+    quant::tensor_cast_kernel<XT, YT><<<cast_grid, quant::kThreads, 0, s>>>(a);
+    return check_launch("tensor_cast_kernel");
+  });
+}
+
+int pcb_pack_u8(const void* src, int64_t batch, int64_t rows, int64_t cols, int64_t ssb, int64_t ssr, int64_t ssc,
+                void* dst, int64_t dsb, int64_t dsr, int64_t cols_padded, void* stream) {
+  if (batch < 0 || rows < 0 || cols < 0 || cols_padded < cols) return fail(PCB_ERR_INVALID, "bad pack sizes");
+  const int64_t total = batch * rows * cols_padded;
+  if (total == 0) return PCB_OK;
+  if (!src || !dst) return fail(PCB_ERR_INVALID, "null pointer");
+  const DeviceInfo di = device_info();
+  const int64_t grid = std::min<int64_t>((total + quant::kThreads - 1) / quant::kThreads, (int64_t)di.sm_count * 8);
+  quant::pack_u8_kernel<<<(unsigned)grid, quant::kThreads, 0, (cudaStream_t)stream>>>(
+      static_cast<const uint8_t*>(src), batch, rows, cols, ssb, ssr, ssc, static_cast<uint8_t*>(dst), dsb, dsr,
+      cols_padded);
+  return check_launch("pack_u8_kernel");
+}
+
+int pcb_bmm_scaled(const void* a, int64_t sab, int64_t sam, int64_t sak, const void* b, int64_t sbb, int64_t sbk,
+                   int64_t sbn, int ab_dtype, int64_t batch, int64_t m, int64_t n, int64_t k, const float* scale_a,
+                   int64_t ssab, int64_t ssam, int64_t ssak, int64_t qbm, const float* scale_b, int64_t ssbb,
+                   int64_t ssbk, int64_t ssbn, int64_t qbn, int64_t qbk, const void* bias, int bias_dtype,
+                   int64_t sbib, int64_t sbim, int64_t sbin, void* c, int c_dtype, int64_t scb, int64_t scm,
+                   int64_t scn, int activation, void* stream) {
+  if (batch < 0 || m < 0 || n < 0 || k < 0) return fail(PCB_ERR_INVALID, "negative size");
+  if (!is_fp8(ab_dtype)) return fail(PCB_ERR_INVALID, "A/B dtype must be E4M3 or E5M2");
+  if (elem_size(c_dtype) == 0) return fail(PCB_ERR_INVALID, "bad output dtype");
+  if (bias && !is_float_in(bias_dtype)) return fail(PCB_ERR_INVALID, "bias dtype must be F32/F16/BF16");
+  if (activation != PCB_ACT_NONE && activation != PCB_ACT_GELU) return fail(PCB_ERR_INVALID, "bad activation");
+  if (qbm <= 0 || qbn <= 0 || qbk <= 0) return fail(PCB_ERR_INVALID, "quant block sizes must be positive");
+  if (batch == 0 || m == 0 || n == 0) return PCB_OK;
+  if (!c || (k > 0 && (!a || !b))) return fail(PCB_ERR_INVALID, "null pointer");
+  if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX || batch > 65535)
+    return fail(PCB_ERR_UNSUPPORTED, "dimension too large");
+  if (scn != 1) return fail(PCB_ERR_LAYOUT, "output must be contiguous along N");
+  const DeviceInfo di = device_info();
+  if (di.major != 10) return fail(PCB_ERR_DEVICE, "pcb_bmm_scaled needs an sm_100 device");
+
+  const int64_t k_stages = (k + gemm::BK - 1) / gemm::BK;
+  int64_t spg;
+  if (qbk >= k) {
+    spg = std::max<int64_t>(1, k_stages);
+  } else {
+    if (qbk % gemm::BK != 0) return fail(PCB_ERR_UNSUPPORTED, "qbk must be a multiple of 128 or >= K");
+    spg = qbk / gemm::BK;
+  }
+
+  // Operand layouts (bytes == elements for fp8).
+  bool a_mn = false, b_mn = false;
+  CUtensorMap ta, tb;
+  const int bn = 128;  // see below
+  if (k == 0) {
+    // No K stages: the kernel only writes bias/zeros; the maps are never read.
+    std::memset(&ta, 0, sizeof(ta));
+    std::memset(&tb, 0, sizeof(tb));
+  } else {
+  if (sak == 1) {
+    a_mn = false;
+    if (sam % 16 != 0) return fail(PCB_ERR_LAYOUT, "K-major A row stride must be a multiple of 16 bytes");
+  } else if (sam == 1) {
+    a_mn = true;
+    if (sak % 16 != 0) return fail(PCB_ERR_LAYOUT, "M-major A stride must be a multiple of 16 bytes");
+  } else {
+    return fail(PCB_ERR_LAYOUT, "A must be contiguous along K or M");
+  }
+  if (sbk == 1) {
+    b_mn = false;
+    if (sbn % 16 != 0) return fail(PCB_ERR_LAYOUT, "K-major B stride must be a multiple of 16 bytes");
+  } else if (sbn == 1) {
+    b_mn = true;
+    if (sbk % 16 != 0) return fail(PCB_ERR_LAYOUT, "N-major B stride must be a multiple of 16 bytes");
+  } else {
+    return fail(PCB_ERR_LAYOUT, "B must be contiguous along K or N");
+  }
+  if (batch > 1 && (sab % 16 != 0 || sbb % 16 != 0)) return fail(PCB_ERR_LAYOUT, "batch strides must be multiples of 16 bytes");
+  if (k > 0 && (!aligned(a, 16) || !aligned(b, 16))) return fail(PCB_ERR_LAYOUT, "A/B must be 16-byte aligned");
+
+  const uint64_t kk = (uint64_t)k;
+  bool okA = a_mn ? make_map_u8(&ta, a, (uint64_t)m, kk, (uint64_t)batch, (uint64_t)sak, (uint64_t)sab, 128)
+                  : make_map_u8(&ta, a, kk, (uint64_t)m, (uint64_t)batch, (uint64_t)sam, (uint64_t)sab, 128);
+  bool okB = b_mn ? make_map_u8(&tb, b, (uint64_t)n, kk, (uint64_t)batch, (uint64_t)sbk, (uint64_t)sbb, 128)
+                  : make_map_u8(&tb, b, kk, (uint64_t)n, (uint64_t)batch, (uint64_t)sbn, (uint64_t)sbb,
+                                (uint32_t)bn);
+  if (!okA || !okB) return fail(PCB_ERR_LAYOUT, "cuTensorMapEncodeTiled rejected the operand layout");
+  }
+  // 128x128 tiles: two epilogue warpgroups hold 64 fp32 accumulators per
+  // thread without spilling (a 128x256 tile would need 128 per thread).
+  const int epi_cols = bn / 2;
+
+  gemm::Params p{};
+  p.batch = (int)batch;
+  p.m = (int)m;
+  p.n = (int)n;
+  p.k = (int)k;
+  p.m_blocks = (int)((m + gemm::BM - 1) / gemm::BM);
+  p.n_blocks = (int)((n + bn - 1) / bn);
+  p.num_tiles = (int)(batch * p.m_blocks * p.n_blocks);
+  p.k_stages = (int)k_stages;
+  p.stages_per_group = (int)spg;
+  p.num_groups = (int)((k_stages + spg - 1) / spg);
+  p.sa = scale_a;
+  p.ssab = ssab;
+  p.ssam = ssam;
+  p.ssak = ssak;
+  p.qbm = (int)std::min<int64_t>(qbm, INT32_MAX);
+  p.sb = scale_b;
+  p.ssbb = ssbb;
+  p.ssbk = ssbk;
+  p.ssbn = ssbn;
+  p.qbn = (int)std::min<int64_t>(qbn, INT32_MAX);
+  p.col_uniform = (!scale_b || ssbn == 0 || qbn % epi_cols == 0 || qbn >= n) ? 1 : 0;
+  p.c = c;
+  p.scb = scb;
+  p.scm = scm;
+  const int ces = elem_size(c_dtype);
+  p.c_dtype = c_dtype;
+  p.c_vec = (aligned(c, 16) && (scm * ces) % 16 == 0 && (batch == 1 || (scb * ces) % 16 == 0)) ? 1 : 0;
+  p.bias = bias;
+  p.sbib = sbib;
+  p.sbim = sbim;
+  p.sbin = sbin;
+  p.bias_dtype = bias_dtype;
+  p.activation = activation;
+  p.inject_error = g_inject_error.exchange(0);
+  const int fmt = (ab_dtype == PCB_DTYPE_E4M3) ? 0 : 1;
+  cudaStream_t s = (cudaStream_t)stream;
+  return dispatch_bmm_layout<128>(a_mn, b_mn, fmt, ta, tb, p, di.sm_count, s);
+}
+
+}  // extern "C"

@@ -1,0 +1,460 @@
+// FP8 quantization kernels (HBM-bound): per-block / per-channel-row groups,
+// per-channel columns (cluster + DSMEM reduction), per-tensor (two launches),
+// and a generic strided fallback.  All produce bytes identical to the torch
+// CPU restatement (see common.cuh for the scale arithmetic).
+#pragma once
+
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+
+namespace pcb {
+namespace quant {
+
+namespace cg = cooperative_groups;
+
+constexpr int kThreads = 256;
+
+enum ScaleMode : int {
+  kDeqReciprocal = 0,  // dequant = 1 / quant_scale     (per-block, per-tensor)
+  kDeqDivide = 1,      // dequant = amax / fp8_max       (per-channel)
+};
+
+struct GroupArgs {
+  const void* x;
+  int64_t sxb, sxm;  // x strides (elements); x is contiguous along n
+  void* y;
+  int64_t syb, sym;  // y strides (elements); y is contiguous along n
+  float* scale;
+  int64_t ssb, ssm, ssn;
+  int64_t batch, m, n;
+  int64_t gm, gn;        // group extent (rows, cols)
+  int64_t groups_m, groups_n;
+  int64_t num_groups;
+  float eps;
+};
+
+// 16-byte chunk of input converted to VEC floats.
+template <int XT>
+struct Chunk {
+  using T = typename InType<XT>::T;
+  static constexpr int VEC = 16 / (int)sizeof(T);
+  float v[VEC];
+  __device__ __forceinline__ void load(const T* p) {
+    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p));
+    const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) v[i] = InType<XT>::to_f32(e[i]);
+  }
+  __device__ __forceinline__ uint32_t amax_bits() const {
+    uint32_t a = 0;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) a = max(a, abs_bits(v[i]));
+    return a;
+  }
+  template <int YT>
+  __device__ __forceinline__ void store(uint8_t* q, float qs) const {
+    if constexpr (VEC == 8) {
+      uint2 out;
+      out.x = (uint32_t)cvt2_fp8<YT>(__fmul_rn(v[0], qs), __fmul_rn(v[1], qs)) |
+              ((uint32_t)cvt2_fp8<YT>(__fmul_rn(v[2], qs), __fmul_rn(v[3], qs)) << 16);
+      out.y = (uint32_t)cvt2_fp8<YT>(__fmul_rn(v[4], qs), __fmul_rn(v[5], qs)) |
+              ((uint32_t)cvt2_fp8<YT>(__fmul_rn(v[6], qs), __fmul_rn(v[7], qs)) << 16);
+      *reinterpret_cast<uint2*>(q) = out;
+    } else {
+      uint32_t out = (uint32_t)cvt2_fp8<YT>(__fmul_rn(v[0], qs), __fmul_rn(v[1], qs)) |
+                     ((uint32_t)cvt2_fp8<YT>(__fmul_rn(v[2], qs), __fmul_rn(v[3], qs)) << 16);
+      *reinterpret_cast<uint32_t*>(q) = out;
+    }
+  }
+};
+
+// Max-reduce `v` over a team of TEAM consecutive threads (TEAM a power of two
+// <= 256).  Teams of <= 32 stay inside a warp; larger teams use `red` (one
+// slot per warp of the CTA).
+template <int TEAM>
+__device__ __forceinline__ uint32_t team_max(uint32_t v, uint32_t* red) {
+  if constexpr (TEAM <= 32) {
+#pragma unroll
+    for (int off = TEAM / 2; off > 0; off >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, off));
+    return v;
+  } else {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, off));
+    constexpr int WARPS = TEAM / 32;
+    const int warp = threadIdx.x >> 5;
+    const int team_warp0 = (warp / WARPS) * WARPS;
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) red[warp] = v;
+    __syncthreads();
+    uint32_t r = 0;
+#pragma unroll
+    for (int w = 0; w < WARPS; ++w) r = max(r, red[team_warp0 + w]);
+    __syncthreads();
+    return r;
+  }
+}
+
+// One team of TEAM threads per quant group; each thread keeps up to CH
+// 16-byte chunks in registers (larger groups re-read the remainder from L2).
+// Grid-strided over groups.  Requires: x, y contiguous along n, 16-byte
+// aligned rows of x, VEC-byte aligned rows of y, n % VEC == 0.
+template <int XT, int YT, int TEAM, int CH, int MODE>
+__global__ void __launch_bounds__(kThreads) quant_groups_kernel(const GroupArgs args) {
+  using C = Chunk<XT>;
+  using T = typename C::T;
+  constexpr int VEC = C::VEC;
+  constexpr int TEAMS_PER_CTA = kThreads / TEAM;
+  __shared__ uint32_t red[kThreads / 32];
+
+  const int t = threadIdx.x % TEAM;
+  const int team_in_cta = threadIdx.x / TEAM;
+  const int64_t team_stride = (int64_t)gridDim.x * TEAMS_PER_CTA;
+  const float fp8_max = Fp8Max<YT>::value;
+  const T* __restrict__ xbase = static_cast<const T*>(args.x);
+  uint8_t* __restrict__ ybase = static_cast<uint8_t*>(args.y);
+
+  // All teams of a CTA run the same number of iterations so the CTA-wide
+  // reduction (TEAM > 32) never diverges around __syncthreads.
+  const int64_t iters = (args.num_groups + team_stride - 1) / team_stride;
+  for (int64_t it = 0; it < iters; ++it) {
+    const int64_t g = it * team_stride + (int64_t)blockIdx.x * TEAMS_PER_CTA + team_in_cta;
+    const bool active = g < args.num_groups;
+    int64_t b = 0, gi = 0, gj = 0, row0 = 0, col0 = 0;
+    int rows = 0, cpr = 1, nch = 0;
+    if (active) {
+      b = g / (args.groups_m * args.groups_n);
+      const int64_t rem = g - b * args.groups_m * args.groups_n;
+      gi = rem / args.groups_n;
+      gj = rem - gi * args.groups_n;
+      row0 = gi * args.gm;
+      col0 = gj * args.gn;
+      rows = (int)min(args.gm, args.m - row0);
+      cpr = (int)(min(args.gn, args.n - col0) / VEC);
+      nch = rows * cpr;
+    }
+    const T* xg = xbase + b * args.sxb + row0 * args.sxm + col0;
+    uint8_t* yg = ybase + b * args.syb + row0 * args.sym + col0;
+
+    C reg[CH];
+    uint32_t amax = 0;
+#pragma unroll
+    for (int i = 0; i < CH; ++i) {
+      const int c = i * TEAM + t;
+      if (c < nch) {
+        const int r = c / cpr;
+        const int cc = c - r * cpr;
+        reg[i].load(xg + r * args.sxm + cc * VEC);
+        amax = max(amax, reg[i].amax_bits());
+      }
+    }
+    for (int c = CH * TEAM + t; c < nch; c += TEAM) {  // groups larger than the register tile
+      const int r = c / cpr;
+      const int cc = c - r * cpr;
+      C tmp;
+      tmp.load(xg + r * args.sxm + cc * VEC);
+      amax = max(amax, tmp.amax_bits());
+    }
+    amax = team_max<TEAM>(amax, red);
+
+    const float safe = clamp_min_eps(__uint_as_float(amax), args.eps);
+    const float qs = quant_scale_from_amax(safe, fp8_max);
+    if (active && t == 0) {
+      const float deq = (MODE == kDeqReciprocal) ? __frcp_rn(qs) : __fdiv_rn(safe, fp8_max);
+      args.scale[b * args.ssb + gi * args.ssm + gj * args.ssn] = deq;
+    }
+#pragma unroll
+    for (int i = 0; i < CH; ++i) {
+      const int c = i * TEAM + t;
+      if (c < nch) {
+        const int r = c / cpr;
+        const int cc = c - r * cpr;
+        reg[i].template store<YT>(yg + r * args.sym + cc * VEC, qs);
+      }
+    }
+    for (int c = CH * TEAM + t; c < nch; c += TEAM) {
+      const int r = c / cpr;
+      const int cc = c - r * cpr;
+      C tmp;
+      tmp.load(xg + r * args.sxm + cc * VEC);
+      tmp.template store<YT>(yg + r * args.sym + cc * VEC, qs);
+    }
+  }
+}
+
+// Generic fallback: one CTA per group, scalar strided loads, two passes.
+struct GenericArgs {
+  const void* x;
+  int64_t sxb, sxm, sxn;
+  void* y;
+  int64_t syb, sym, syn;
+  float* scale;
+  int64_t ssb, ssm, ssn;
+  int64_t batch, m, n;
+  int64_t gm, gn, groups_m, groups_n, num_groups;
+  float eps;
+};
+
+template <int XT, int YT, int MODE>
+__global__ void __launch_bounds__(kThreads) quant_groups_generic_kernel(const GenericArgs args) {
+  using T = typename InType<XT>::T;
+  __shared__ uint32_t red[kThreads / 32];
+  const float fp8_max = Fp8Max<YT>::value;
+  const T* xbase = static_cast<const T*>(args.x);
+  uint8_t* ybase = static_cast<uint8_t*>(args.y);
+  for (int64_t g = blockIdx.x; g < args.num_groups; g += gridDim.x) {
+    const int64_t b = g / (args.groups_m * args.groups_n);
+    const int64_t rem = g - b * args.groups_m * args.groups_n;
+    const int64_t gi = rem / args.groups_n;
+    const int64_t gj = rem - gi * args.groups_n;
+    const int64_t row0 = gi * args.gm, col0 = gj * args.gn;
+    const int64_t rows = min(args.gm, args.m - row0);
+    const int64_t cols = min(args.gn, args.n - col0);
+    const int64_t count = rows * cols;
+    uint32_t amax = 0;
+    for (int64_t e = threadIdx.x; e < count; e += kThreads) {
+      const int64_t r = e / cols, c = e - (e / cols) * cols;
+      const T v = xbase[b * args.sxb + (row0 + r) * args.sxm + (col0 + c) * args.sxn];
+      amax = max(amax, abs_bits(InType<XT>::to_f32(v)));
+    }
+    amax = team_max<kThreads>(amax, red);
+    const float safe = clamp_min_eps(__uint_as_float(amax), args.eps);
+    const float qs = quant_scale_from_amax(safe, fp8_max);
+    if (threadIdx.x == 0) {
+      const float deq = (MODE == kDeqReciprocal) ? __frcp_rn(qs) : __fdiv_rn(safe, fp8_max);
+      args.scale[b * args.ssb + gi * args.ssm + gj * args.ssn] = deq;
+    }
+    for (int64_t e = threadIdx.x; e < count; e += kThreads) {
+      const int64_t r = e / cols, c = e - (e / cols) * cols;
+      const float v =
+          InType<XT>::to_f32(xbase[b * args.sxb + (row0 + r) * args.sxm + (col0 + c) * args.sxn]);
+      ybase[b * args.syb + (row0 + r) * args.sym + (col0 + c) * args.syn] =
+          cvt1_fp8<YT>(__fmul_rn(v, qs));
+    }
+  }
+}
+
+// Per-channel column quantization (one scale per column; reduce over rows) for
+// row-major x.  A cluster of CL CTAs shares one strip of 8*VEC columns, each
+// CTA taking a slice of the rows; the column amax is combined through
+// distributed shared memory, then every CTA quantizes its slice (second read
+// hits L2).
+struct ColArgs {
+  const void* x;
+  int64_t sxb, sxm;
+  void* y;
+  int64_t syb, sym;
+  float* scale;
+  int64_t ssb, ssc;
+  int64_t m, n;
+  int rows_per_cta;
+  float eps;
+};
+
+template <int XT, int YT>
+__global__ void __launch_bounds__(kThreads) quant_cols_cluster_kernel(const ColArgs args) {
+  using C = Chunk<XT>;
+  using T = typename C::T;
+  constexpr int VEC = C::VEC;
+  constexpr int CHUNK_COLS = 8;               // chunks across the strip
+  constexpr int SW = CHUNK_COLS * VEC;        // strip width in columns
+  constexpr int ROW_LANES = kThreads / CHUNK_COLS;  // 32
+  __shared__ uint32_t red[ROW_LANES][SW + 1];
+  __shared__ uint32_t partial[SW];
+  __shared__ float qs_s[SW];
+
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int nranks = (int)cluster.num_blocks();
+  const float fp8_max = Fp8Max<YT>::value;
+
+  const int64_t b = blockIdx.z;
+  const int64_t col0 = (int64_t)blockIdx.x * SW;
+  const int cc = threadIdx.x % CHUNK_COLS;
+  const int rl = threadIdx.x / CHUNK_COLS;
+  const int64_t col = col0 + (int64_t)cc * VEC;
+  const bool col_ok = col < args.n;  // n % VEC == 0, so a chunk is all-in or all-out
+  const int64_t r_begin = (int64_t)rank * args.rows_per_cta;
+  const int64_t r_end = min(args.m, r_begin + args.rows_per_cta);
+  const T* xb = static_cast<const T*>(args.x) + b * args.sxb;
+  uint8_t* yb = static_cast<uint8_t*>(args.y) + b * args.syb;
+
+  uint32_t am[VEC];
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) am[i] = 0;
+  if (col_ok) {
+    for (int64_t r = r_begin + rl; r < r_end; r += ROW_LANES) {
+      C ch;
+      ch.load(xb + r * args.sxm + col);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) am[i] = max(am[i], abs_bits(ch.v[i]));
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) red[rl][cc * VEC + i] = am[i];
+  __syncthreads();
+  if (threadIdx.x < SW) {
+    uint32_t v = 0;
+    for (int l = 0; l < ROW_LANES; ++l) v = max(v, red[l][threadIdx.x]);
+    partial[threadIdx.x] = v;
+  }
+  cluster.sync();
+  if (threadIdx.x < SW) {
+    uint32_t v = 0;
+    for (int r = 0; r < nranks; ++r) v = max(v, cluster.map_shared_rank(partial, r)[threadIdx.x]);
+    const float safe = clamp_min_eps(__uint_as_float(v), args.eps);
+    const float qs = quant_scale_from_amax(safe, fp8_max);
+    qs_s[threadIdx.x] = qs;
+    const int64_t c = col0 + threadIdx.x;
+    if (rank == 0 && c < args.n) args.scale[b * args.ssb + c * args.ssc] = __fdiv_rn(safe, fp8_max);
+  }
+  cluster.sync();  // remote reads of `partial` are done; qs_s visible to the CTA
+  if (col_ok) {
+    for (int64_t r = r_begin + rl; r < r_end; r += ROW_LANES) {
+      C ch;
+      ch.load(xb + r * args.sxm + col);
+      // Chunk::store takes one scale; columns differ, so convert pairwise here.
+      uint8_t out[VEC];
+#pragma unroll
+      for (int i = 0; i < VEC; i += 2) {
+        const uint16_t p = cvt2_fp8<YT>(__fmul_rn(ch.v[i], qs_s[cc * VEC + i]),
+                                        __fmul_rn(ch.v[i + 1], qs_s[cc * VEC + i + 1]));
+        out[i] = (uint8_t)(p & 0xff);
+        out[i + 1] = (uint8_t)(p >> 8);
+      }
+      if constexpr (VEC == 8) {
+        *reinterpret_cast<uint2*>(yb + r * args.sym + col) = *reinterpret_cast<const uint2*>(out);
+      } else {
+        *reinterpret_cast<uint32_t*>(yb + r * args.sym + col) = *reinterpret_cast<const uint32_t*>(out);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Per-tensor: (1) per-CTA amax partials, (2) every CTA of the cast kernel
+// reduces the partials (deterministic), derives the scale in `scale_dtype`
+// arithmetic and quantizes its share; CTA 0 writes the two scale outputs.
+// ---------------------------------------------------------------------------
+struct TensorArgs {
+  const void* x;
+  int64_t sxb, sxm, sxn;
+  void* y;
+  int64_t syb, sym, syn;
+  int64_t batch, m, n;
+  bool vec;  // contiguous along n, aligned, n % VEC == 0
+  float* partials;
+  int num_partials;
+  float* quant_scale;
+  float* dequant_scale;
+  int scale_dtype;
+  float fp8_max;
+  float eps;
+};
+
+constexpr int kPerTensorMaxPartials = 1024;
+
+__device__ __forceinline__ float round_to(float v, int dt) {
+  if (dt == PCB_DTYPE_BF16) return __bfloat162float(__float2bfloat16_rn(v));
+  if (dt == PCB_DTYPE_F16) return __half2float(__float2half_rn(v));
+  return v;
+}
+
+template <int XT>
+__global__ void __launch_bounds__(kThreads) tensor_amax_kernel(const TensorArgs args) {
+  using C = Chunk<XT>;
+  using T = typename C::T;
+  constexpr int VEC = C::VEC;
+  __shared__ uint32_t red[kThreads / 32];
+  const T* xb = static_cast<const T*>(args.x);
+  uint32_t amax = 0;
+  const int64_t rows = args.batch * args.m;
+  const int64_t tid = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * kThreads;
+  if (args.vec) {
+    const int64_t cpr = args.n / VEC;
+    const int64_t total = rows * cpr;
+    for (int64_t c = tid; c < total; c += stride) {
+      const int64_t row = c / cpr;
+      const int64_t bi = row / args.m, r = row - bi * args.m;
+      C ch;
+      ch.load(xb + bi * args.sxb + r * args.sxm + (c - row * cpr) * VEC);
+      amax = max(amax, ch.amax_bits());
+    }
+  } else {
+    const int64_t total = rows * args.n;
+    for (int64_t e = tid; e < total; e += stride) {
+      const int64_t row = e / args.n;
+      const int64_t bi = row / args.m, r = row - bi * args.m;
+      amax = max(amax, abs_bits(InType<XT>::to_f32(xb[bi * args.sxb + r * args.sxm + (e - row * args.n) * args.sxn])));
+    }
+  }
+  amax = team_max<kThreads>(amax, red);
+  if (threadIdx.x == 0) args.partials[blockIdx.x] = __uint_as_float(amax);
+}
+
+template <int XT, int YT>
+__global__ void __launch_bounds__(kThreads) tensor_cast_kernel(const TensorArgs args) {
+  using C = Chunk<XT>;
+  using T = typename C::T;
+  constexpr int VEC = C::VEC;
+  __shared__ uint32_t red[kThreads / 32];
+  uint32_t amax = 0;
+  for (int i = threadIdx.x; i < args.num_partials; i += kThreads)
+    amax = max(amax, __float_as_uint(args.partials[i]));
+  amax = team_max<kThreads>(amax, red);
+  // x_max_abs.clamp(min=eps) -> fp8_max / x -> reciprocal, all in scale_dtype.
+  const int dt = args.scale_dtype;
+  const float a = __uint_as_float(amax);
+  const float eps_dt = round_to(args.eps, dt);
+  const float safe = (a < eps_dt) ? eps_dt : a;
+  const float qs = round_to(__fmul_rn(round_to(__frcp_rn(safe), dt), args.fp8_max), dt);
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    if (args.quant_scale) *args.quant_scale = qs;
+    if (args.dequant_scale) *args.dequant_scale = round_to(__frcp_rn(qs), dt);
+  }
+  const T* xb = static_cast<const T*>(args.x);
+  uint8_t* yb = static_cast<uint8_t*>(args.y);
+  const int64_t rows = args.batch * args.m;
+  const int64_t tid = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * kThreads;
+  if (args.vec) {
+    const int64_t cpr = args.n / VEC;
+    const int64_t total = rows * cpr;
+    for (int64_t c = tid; c < total; c += stride) {
+      const int64_t row = c / cpr;
+      const int64_t bi = row / args.m, r = row - bi * args.m;
+      const int64_t col = (c - row * cpr) * VEC;
+      C ch;
+      ch.load(xb + bi * args.sxb + r * args.sxm + col);
+      ch.template store<YT>(yb + bi * args.syb + r * args.sym + col, qs);
+    }
+  } else {
+    const int64_t total = rows * args.n;
+    for (int64_t e = tid; e < total; e += stride) {
+      const int64_t row = e / args.n;
+      const int64_t bi = row / args.m, r = row - bi * args.m;
+      const int64_t col = e - row * args.n;
+      const float v = InType<XT>::to_f32(xb[bi * args.sxb + r * args.sxm + col * args.sxn]);
+      yb[bi * args.syb + r * args.sym + col * args.syn] = cvt1_fp8<YT>(__fmul_rn(v, qs));
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Byte repack (layout change / zero padding) for fp8 operands.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads) pack_u8_kernel(const uint8_t* src, int64_t batch, int64_t rows,
+                                                           int64_t cols, int64_t ssb, int64_t ssr, int64_t ssc,
+                                                           uint8_t* dst, int64_t dsb, int64_t dsr, int64_t cols_padded) {
+  const int64_t total = batch * rows * cols_padded;
+  for (int64_t e = (int64_t)blockIdx.x * kThreads + threadIdx.x; e < total; e += (int64_t)gridDim.x * kThreads) {
+    const int64_t row = e / cols_padded;
+    const int64_t c = e - row * cols_padded;
+    const int64_t bi = row / rows, r = row - bi * rows;
+    dst[bi * dsb + r * dsr + c] = (c < cols) ? src[bi * ssb + r * ssr + c * ssc] : (uint8_t)0;
+  }
+}
+
+}  // namespace quant
+}  // namespace pcb
