@@ -52,6 +52,8 @@ def parse_args():
     ap.add_argument("--batches", type=int, default=GLOBAL_B, help="global batch count (cfg3: 32)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--fp8-peak", action="store_true",
+                    help="only measure the FP8 dense peak with torch._scaled_mm (cuBLASLt) at 8192^3")
     return ap.parse_args()
 
 
@@ -224,9 +226,55 @@ def workload_config(args) -> dict:
     }
 
 
+def measure_fp8_peak() -> None:
+    """torch._scaled_mm e4m3 8192^3: best of 10 (burst) and back-to-back for
+    4 s (sustained), the protocol of MEASURED_PEAKS.json's bf16 entry."""
+    n = 8192
+    dev = torch.device("cuda", 0)
+    a = torch.randn((n, n), device=dev).to(torch.float8_e4m3fn)
+    b = torch.randn((n, n), device=dev).to(torch.float8_e4m3fn).t()
+    one = torch.ones((), device=dev)
+
+    def mm():
+        return torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+
+    for _ in range(5):
+        mm()
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(10):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        mm()
+        e.record()
+        torch.cuda.synchronize()
+        best = min(best, s.elapsed_time(e))
+    flop = 2 * n ** 3
+    clocks = ClockSampler(0)
+    clocks.start()
+    iters, t0 = 0, time.perf_counter()
+    s = torch.cuda.Event(enable_timing=True)
+    s.record()
+    while time.perf_counter() - t0 < 4.0:
+        for _ in range(20):
+            mm()
+        iters += 20
+        torch.cuda.synchronize()
+    e = torch.cuda.Event(enable_timing=True)
+    e.record()
+    torch.cuda.synchronize()
+    sustained_ms = s.elapsed_time(e) / iters
+    print(json.dumps({"fp8_e4m3_scaled_mm_tflops_burst": flop / (best * 1e-3) / 1e12,
+                      "fp8_e4m3_scaled_mm_tflops_sustained": flop / (sustained_ms * 1e-3) / 1e12,
+                      "shape": [n, n, n], "clocks": clocks.stop(), "how": "torch._scaled_mm (cuBLASLt) e4m3, bf16 out"}))
+
+
 # ------------------------------------------------------------------- main ---
 def main() -> None:
     args = parse_args()
+    if args.fp8_peak:
+        measure_fp8_peak()
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
