@@ -124,6 +124,34 @@ int pcb_quant_per_tensor(const void* x, int x_dtype, int64_t batch, int64_t m, i
                          float fp8_max, float eps, float* workspace, void* stream);
 
 /*
+ * Per-tensor quantization that allocates nothing -- not even the small
+ * workspace pcb_quant_per_tensor asks for.  No counterpart in the reference:
+ * it exists for callers that cannot hand the library a scratch buffer, such
+ * as a plugin slot whose host framework passes only the input and output
+ * tensors, or a latency-critical loop that must not call cudaMalloc (which
+ * can synchronise the whole device).  Same arguments, results and scale
+ * semantics as pcb_quant_per_tensor, minus `workspace`.
+ *
+ * Scratch: the amax partials live in a 1024-slot fp32 array (4 KiB) compiled
+ * into the library; every GPU that loads the library holds it until the
+ * process exits.  The amax pass launches at most four CTAs per SM (592 on a
+ * B200), one slot each, so on such a GPU every tensor size is accepted; a
+ * launch that would need more than the 1024 slots is rejected with
+ * PCB_ERR_INVALID and an explanatory pcb_last_error_text().
+ * The first call on each device looks up that array's device address (with
+ * the device current) and caches it, so make the first call on a device
+ * before any stream capture.  All calls share the one array: two calls whose
+ * kernels overlap on the GPU (e.g. on two streams at once) race and may
+ * return wrong scales; serialise them.  Nothing in the array has to start at
+ * zero: each call writes every slot it later reads.
+ */
+int pcb_quant_per_tensor_noalloc(const void* x, int x_dtype, int64_t batch, int64_t m, int64_t n,
+                                 int64_t sxb, int64_t sxm, int64_t sxn,
+                                 void* y, int y_dtype, int64_t syb, int64_t sym, int64_t syn,
+                                 float* quant_scale, float* dequant_scale, int scale_dtype,
+                                 float fp8_max, float eps, void* stream);
+
+/*
  * Scaled FP8 batched GEMM on the tcgen05 tensor cores:
  *   C[b,m,n] = act( sum_g (sum_{k in g} A[b,m,k] B[b,k,n]) * sa(b,m,g) * sb(b,g,n)
  *                   + bias[b,m,n] )

@@ -58,6 +58,10 @@ _SIGNATURES = {
         _i,
         [_vp, _i, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i, _i64, _i64, _i64, _vp, _vp, _i, _f, _f, _vp, _vp],
     ),
+    "pcb_quant_per_tensor_noalloc": (
+        _i,
+        [_vp, _i, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i, _i64, _i64, _i64, _vp, _vp, _i, _f, _f, _vp],
+    ),
     "pcb_bmm_scaled": (
         _i,
         [_vp, _i64, _i64, _i64,  # a

@@ -207,6 +207,41 @@ int dispatch_bmm_layout(bool a_mn, bool b_mn, int fmt, const CUtensorMap& ta, co
   return launch_bmm<BN, true, true, 1>(ta, tb, p, sm, s);
 }
 
+// ---------------------------------------------------------------------------
+// Scratch for pcb_quant_per_tensor_noalloc.  The per-tensor quantizer reduces
+// the amax in two launches and parks one partial per amax CTA in between;
+// this variant keeps those partials in a fixed array that is part of the
+// library image instead of in caller-provided memory.  Every GPU that loads
+// the library holds these 4 KiB until the process exits.
+// ---------------------------------------------------------------------------
+constexpr int kNoAllocPartials = 1024;  // fp32 slots = the most amax CTAs ever launched
+static __device__ __align__(256) float g_noalloc_partials[kNoAllocPartials];
+
+// Device address of g_noalloc_partials on the current device.  The name is a
+// host-side stand-in in host code, so it must be translated once per device
+// (with that device current) before a kernel may be given it.
+float* noalloc_partials_on_current_device() {
+  static std::mutex mu;
+  static float* addr[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    fail(PCB_ERR_DEVICE, "pcb_quant_per_tensor_noalloc: no current CUDA device");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_partials);
+    if (e != cudaSuccess || p == nullptr) {
+      g_last_error = std::string("pcb_quant_per_tensor_noalloc: cudaGetSymbolAddress failed: ") +
+                     cudaGetErrorString(e);
+      return nullptr;
+    }
+    addr[dev] = static_cast<float*>(p);
+  }
+  return addr[dev];
+}
+
 }  // namespace
 
 extern "C" {
@@ -344,6 +379,48 @@ int pcb_quant_per_tensor(const void* x, int x_dtype, int64_t batch, int64_t m, i
                                                  (int64_t)di.sm_count * 8);
     quant::tensor_cast_kernel<XT, YT><<<cast_grid, quant::kThreads, 0, s>>>(a);
     return check_launch("tensor_cast_kernel");
+  });
+}
+
+int pcb_quant_per_tensor_noalloc(const void* x, int x_dtype, int64_t batch, int64_t m, int64_t n, int64_t sxb,
+                                 int64_t sxm, int64_t sxn, void* y, int y_dtype, int64_t syb, int64_t sym,
+                                 int64_t syn, float* quant_scale, float* dequant_scale, int scale_dtype,
+                                 float fp8_max, float eps, void* stream) {
+  if (batch < 0 || m < 0 || n < 0) return fail(PCB_ERR_INVALID, "negative size");
+  if (!x || !y) return fail(PCB_ERR_INVALID, "null pointer");
+  if (!is_float_in(x_dtype) || !is_fp8(y_dtype) || !is_float_in(scale_dtype)) return fail(PCB_ERR_INVALID, "bad dtype");
+  float* partials = noalloc_partials_on_current_device();
+  if (!partials) return PCB_ERR_DEVICE;
+  cudaStream_t s = (cudaStream_t)stream;
+  const DeviceInfo di = device_info();
+  const int es = elem_size(x_dtype);
+  const int vec = 16 / es;
+  const bool vec_ok = sxn == 1 && syn == 1 && n % vec == 0 && aligned(x, 16) && (sxm * es) % 16 == 0 &&
+                      (batch == 1 || (sxb * es) % 16 == 0) && aligned(y, vec) && sym % vec == 0 &&
+                      (batch == 1 || syb % vec == 0);
+  const int64_t total = batch * m * n;
+  const int64_t per_cta = (int64_t)quant::kThreads * (vec_ok ? vec : 1);
+  const int64_t wanted = std::min<int64_t>(std::max<int64_t>(1, (total + per_cta - 1) / per_cta),
+                                           (int64_t)di.sm_count * 4);
+  if (wanted > kNoAllocPartials)
+    return fail(PCB_ERR_INVALID,
+                "pcb_quant_per_tensor_noalloc: the launch needs more amax partial slots than the "
+                "1024-slot static scratch holds");
+  const int amax_grid = (int)wanted;
+  // Every partial slot the cast kernel reads (0 .. amax_grid-1) is written by
+  // the amax kernel of this same call, so nothing needs clearing first.
+  quant::TensorArgs a{x, sxb, sxm, sxn, y, syb, sym, syn, batch, m, n, vec_ok, partials, amax_grid,
+                      quant_scale, dequant_scale, scale_dtype, fp8_max, eps};
+  return dispatch_xy(x_dtype, y_dtype, [&](auto xc, auto yc) -> int {
+    constexpr int XT = decltype(xc)::value;
+    constexpr int YT = decltype(yc)::value;
+    quant::tensor_amax_kernel<XT><<<amax_grid, quant::kThreads, 0, s>>>(a);
+    int st = check_launch("tensor_amax_kernel (noalloc)");
+    if (st != PCB_OK) return st;
+    const int cast_grid = (int)std::min<int64_t>(std::max<int64_t>(1, (total + per_cta - 1) / per_cta),
+                                                 (int64_t)di.sm_count * 8);
+    quant::tensor_cast_kernel<XT, YT><<<cast_grid, quant::kThreads, 0, s>>>(a);
+    return check_launch("tensor_cast_kernel (noalloc)");
   });
 }
 
