@@ -24,6 +24,8 @@ constexpr int UMMA_K = 32;        // K per tcgen05.mma for 8-bit inputs
 constexpr int kThreads = 384;
 constexpr int kEpiWarp0 = 4;
 constexpr int kEpiThreads = 256;
+constexpr int kNumAcc = 4;        // TMEM accumulator buffers of BN fp32 columns
+constexpr int kScalePrefetch = 4;  // K groups of scales kept in flight per epilogue thread
 
 struct Params {
   int batch, m, n, k;
@@ -96,9 +98,8 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
                : "memory");
 }
 
-// 32 consecutive fp32 columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
+// 32 consecutive fp32 columns of this thread's TMEM lane (no wait).
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
       "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -108,10 +109,9 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
         "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // UMMA shared-memory descriptor for a 128-byte-swizzled tile.
 //   K-major : rows of 128 bytes (BK fp8), 8-row atoms 1024 B apart (SBO).
@@ -143,7 +143,7 @@ struct Smem {
   static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
   static constexpr int OFF_COLSCALE = OFF_B + STAGES * B_BYTES;           // 8 warps x EPI_COLS floats
   static constexpr int OFF_BAR = OFF_COLSCALE + 8 * EPI_COLS * 4;
-  static constexpr int NUM_BARS = 2 * STAGES + 4;
+  static constexpr int NUM_BARS = 2 * STAGES + 2 * kNumAcc;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;                  // tmem addr, abort flag
   static constexpr int BYTES = OFF_MISC + 16;
   static constexpr int ALLOC = BYTES + 1024;                              // slack for 1 KB alignment
@@ -157,14 +157,15 @@ __device__ __forceinline__ float load_bias(const void* p, int dt, long long off)
   return __half2float(static_cast<const __half*>(p)[off]);
 }
 
-template <int BN, bool A_MN, bool B_MN, int AB_FMT>
+template <int BN, bool A_MN, bool B_MN, int AB_FMT, bool COL_UNIFORM>
 __global__ void __launch_bounds__(kThreads, 1)
     bmm_scaled_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                       const Params p) {
   using S = Smem<BN>;
   constexpr int STAGES = S::STAGES;
   constexpr int EPI_COLS = S::EPI_COLS;
-  constexpr uint32_t TMEM_COLS = 2 * BN;
+  constexpr uint32_t TMEM_COLS = kNumAcc * BN;
+  static_assert(kNumAcc * BN <= 512, "TMEM holds 512 fp32 columns");
   constexpr uint32_t IDESC = make_idesc(BN, AB_FMT, A_MN ? 1 : 0, B_MN ? 1 : 0);
   constexpr uint32_t STAGE_TX = S::A_BYTES + S::B_BYTES;
 
@@ -173,8 +174,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t s_base = smem_u32(smem);
   const uint32_t bar_full = s_base + S::OFF_BAR;                  // [STAGES]
   const uint32_t bar_empty = bar_full + 8 * STAGES;               // [STAGES]
-  const uint32_t bar_tfull = bar_empty + 8 * STAGES;              // [2]
-  const uint32_t bar_tempty = bar_tfull + 16;                     // [2]
+  const uint32_t bar_tfull = bar_empty + 8 * STAGES;              // [kNumAcc]
+  const uint32_t bar_tempty = bar_tfull + 8 * kNumAcc;            // [kNumAcc]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 4);
 
@@ -186,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar_full + 8 * s, 1);
       mbar_init(bar_empty + 8 * s, 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kNumAcc; ++i) {
       mbar_init(bar_tfull + 8 * i, 1);
       mbar_init(bar_tempty + 8 * i, 8);  // one arrive per epilogue warp
     }
@@ -257,8 +258,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
         for (int g = 0; g < p.num_groups && ok; ++g) {
-          const uint32_t abuf = acc_cnt & 1;
-          const uint32_t aphase = (acc_cnt >> 1) & 1;
+          const uint32_t abuf = acc_cnt % kNumAcc;
+          const uint32_t aphase = (acc_cnt / kNumAcc) & 1;
           if (!mbar_wait_bounded(bar_tempty + 8 * abuf, aphase ^ 1, abort_flag, SITE_GEMM_MMA)) {
             ok = false;
             break;
@@ -317,54 +318,89 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float* sa_row = p.sa ? p.sa + (long long)b * p.ssab + (long long)(row / p.qbm) * p.ssam : nullptr;
       const float* sb_b = p.sb ? p.sb + (long long)b * p.ssbb : nullptr;
 
-      float acc[EPI_COLS];
+      float2 acc[EPI_COLS / 2];
 #pragma unroll
-      for (int i = 0; i < EPI_COLS; ++i) acc[i] = 0.f;
+      for (int i = 0; i < EPI_COLS / 2; ++i) acc[i] = make_float2(0.f, 0.f);
 
-      for (int g = 0; g < p.num_groups; ++g) {
-        const uint32_t abuf = acc_cnt & 1;
-        const uint32_t aphase = (acc_cnt >> 1) & 1;
-        // Scales for this group (loaded before the wait to hide latency).
-        const float s_row = (sa_row && row_ok) ? __ldg(sa_row + (long long)g * p.ssak) : 1.f;
-        float s_col = 1.f;
-        if (p.col_uniform) {
-          if (sb_b && col0 < p.n) s_col = __ldg(sb_b + (long long)g * p.ssbk + (long long)(col0 / p.qbn) * p.ssbn);
-        } else {
-          __syncwarp();
+      // Scales of the next kScalePrefetch groups stay in flight in registers
+      // (the group loop is unrolled by kScalePrefetch so the ring indices are static).
+      auto row_scale = [&](int g) -> float {
+        return (sa_row && row_ok) ? __ldg(sa_row + (long long)g * p.ssak) : 1.f;
+      };
+      auto col_scale = [&](int g) -> float {
+        return (COL_UNIFORM && sb_b && col0 < p.n)
+                   ? __ldg(sb_b + (long long)g * p.ssbk + (long long)(col0 / p.qbn) * p.ssbn)
+                   : 1.f;
+      };
+      float rs[kScalePrefetch], cs[kScalePrefetch];
 #pragma unroll
-          for (int i = lane; i < EPI_COLS; i += 32) {
-            const int c = col0 + i;
-            colscale[i] = (sb_b && c < p.n) ? __ldg(sb_b + (long long)g * p.ssbk + (long long)(c / p.qbn) * p.ssbn) : 1.f;
+      for (int j = 0; j < kScalePrefetch; ++j) {
+        rs[j] = (j < p.num_groups) ? row_scale(j) : 1.f;
+        cs[j] = (j < p.num_groups) ? col_scale(j) : 1.f;
+      }
+      for (int g0 = 0; g0 < p.num_groups && ok; g0 += kScalePrefetch) {
+#pragma unroll
+        for (int j = 0; j < kScalePrefetch; ++j) {
+          const int g = g0 + j;
+          if (g >= p.num_groups || !ok) break;
+          const uint32_t abuf = acc_cnt % kNumAcc;
+          const uint32_t aphase = (acc_cnt / kNumAcc) & 1;
+          const float s_row = rs[j];
+          const float s_col = cs[j];
+          if (g + kScalePrefetch < p.num_groups) {
+            rs[j] = row_scale(g + kScalePrefetch);
+            cs[j] = col_scale(g + kScalePrefetch);
           }
+          if constexpr (!COL_UNIFORM) {
+            __syncwarp();
+#pragma unroll
+            for (int i = lane; i < EPI_COLS; i += 32) {
+              const int c = col0 + i;
+              colscale[i] =
+                  (sb_b && c < p.n) ? __ldg(sb_b + (long long)g * p.ssbk + (long long)(c / p.qbn) * p.ssbn) : 1.f;
+            }
+            __syncwarp();
+          }
+          if (!mbar_wait_bounded(bar_tfull + 8 * abuf, aphase, abort_flag, SITE_GEMM_EPILOGUE)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN + half * EPI_COLS;
+          uint32_t v[EPI_COLS / 32][32];
+#pragma unroll
+          for (int c = 0; c < EPI_COLS / 32; ++c) tmem_ld32_nowait(taddr + c * 32, v[c]);
+          tmem_wait_ld();
+          // The accumulator buffer is free as soon as it sits in registers.
+          tc_fence_before();
           __syncwarp();
-        }
-        if (!mbar_wait_bounded(bar_tfull + 8 * abuf, aphase, abort_flag, SITE_GEMM_EPILOGUE)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN + half * EPI_COLS;
-#pragma unroll
-        for (int j = 0; j < EPI_COLS / 32; ++j) {
-          float v[32];
-          tmem_ld32(taddr + j * 32, v);
-          if (p.col_uniform) {
+          if (lane == 0) mbar_arrive(bar_tempty + 8 * abuf);
+          if constexpr (COL_UNIFORM) {
             const float s = s_row * s_col;
+            const float2 s2 = make_float2(s, s);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) acc[j * 32 + i] = fmaf(v[i], s, acc[j * 32 + i]);
+            for (int c = 0; c < EPI_COLS / 32; ++c)
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                acc[c * 16 + i] = __ffma2_rn(make_float2(__uint_as_float(v[c][2 * i]), __uint_as_float(v[c][2 * i + 1])),
+                                             s2, acc[c * 16 + i]);
           } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) acc[j * 32 + i] = fmaf(v[i], s_row * colscale[j * 32 + i], acc[j * 32 + i]);
+            for (int c = 0; c < EPI_COLS / 32; ++c)
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const float2 s2 = make_float2(s_row * colscale[c * 32 + 2 * i], s_row * colscale[c * 32 + 2 * i + 1]);
+                acc[c * 16 + i] = __ffma2_rn(make_float2(__uint_as_float(v[c][2 * i]), __uint_as_float(v[c][2 * i + 1])),
+                                             s2, acc[c * 16 + i]);
+              }
           }
+          ++acc_cnt;
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar_tempty + 8 * abuf);
-        ++acc_cnt;
       }
       if (!ok) break;
 
       // Bias, activation, cast, store.
+      float* accf = reinterpret_cast<float*>(acc);
       if (row_ok) {
         const long long crow = (long long)b * p.scb + (long long)row * p.scm;
         if (p.bias) {
@@ -372,12 +408,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < EPI_COLS; ++i) {
             const int c = col0 + i;
             if (c < p.n)
-              acc[i] += load_bias(p.bias, p.bias_dtype, (long long)b * p.sbib + (long long)row * p.sbim + (long long)c * p.sbin);
+              accf[i] += load_bias(p.bias, p.bias_dtype, (long long)b * p.sbib + (long long)row * p.sbim + (long long)c * p.sbin);
           }
         }
         if (p.activation == PCB_ACT_GELU) {
 #pragma unroll
-          for (int i = 0; i < EPI_COLS; ++i) acc[i] = gelu_erf(acc[i]);
+          for (int i = 0; i < EPI_COLS; ++i) accf[i] = gelu_erf(accf[i]);
         }
         const bool full = p.c_vec && (col0 + EPI_COLS <= p.n);
         if (p.c_dtype == PCB_DTYPE_BF16 || p.c_dtype == PCB_DTYPE_F16) {
@@ -390,10 +426,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
                 if (p.c_dtype == PCB_DTYPE_BF16) {
-                  __nv_bfloat162 h = __floats2bfloat162_rn(acc[i + 2 * q], acc[i + 2 * q + 1]);
+                  __nv_bfloat162 h = __floats2bfloat162_rn(accf[i + 2 * q], accf[i + 2 * q + 1]);
                   wp[q] = *reinterpret_cast<uint32_t*>(&h);
                 } else {
-                  __half2 h = __floats2half2_rn(acc[i + 2 * q], acc[i + 2 * q + 1]);
+                  __half2 h = __floats2half2_rn(accf[i + 2 * q], accf[i + 2 * q + 1]);
                   wp[q] = *reinterpret_cast<uint32_t*>(&h);
                 }
               }
@@ -404,10 +440,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int i = 0; i < EPI_COLS; ++i) {
               if (col0 + i < p.n) {
                 if (p.c_dtype == PCB_DTYPE_BF16) {
-                  __nv_bfloat16 h = __float2bfloat16_rn(acc[i]);
+                  __nv_bfloat16 h = __float2bfloat16_rn(accf[i]);
                   out[i] = *reinterpret_cast<uint16_t*>(&h);
                 } else {
-                  __half h = __float2half_rn(acc[i]);
+                  __half h = __float2half_rn(accf[i]);
                   out[i] = *reinterpret_cast<uint16_t*>(&h);
                 }
               }
@@ -418,18 +454,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (full) {
 #pragma unroll
             for (int i = 0; i < EPI_COLS; i += 4)
-              *reinterpret_cast<float4*>(out + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+              *reinterpret_cast<float4*>(out + i) = make_float4(accf[i], accf[i + 1], accf[i + 2], accf[i + 3]);
           } else {
 #pragma unroll
             for (int i = 0; i < EPI_COLS; ++i)
-              if (col0 + i < p.n) out[i] = acc[i];
+              if (col0 + i < p.n) out[i] = accf[i];
           }
         } else {
           uint8_t* out = static_cast<uint8_t*>(p.c) + crow + col0;
 #pragma unroll
           for (int i = 0; i < EPI_COLS; ++i) {
             if (col0 + i < p.n)
-              out[i] = (p.c_dtype == PCB_DTYPE_E4M3) ? cvt1_fp8<PCB_DTYPE_E4M3>(acc[i]) : cvt1_fp8<PCB_DTYPE_E5M2>(acc[i]);
+              out[i] = (p.c_dtype == PCB_DTYPE_E4M3) ? cvt1_fp8<PCB_DTYPE_E4M3>(accf[i]) : cvt1_fp8<PCB_DTYPE_E5M2>(accf[i]);
           }
         }
       }

@@ -97,6 +97,41 @@ int launch_groups(const void* x, int xt, int64_t batch, int64_t m, int64_t n, in
   const bool vec_ok = sxn == 1 && syn == 1 && n % vec == 0 && gn % vec == 0 && aligned(x, 16) &&
                       (sxm * es) % 16 == 0 && (batch == 1 || (sxb * es) % 16 == 0) && aligned(y, vec) &&
                       sym % vec == 0 && (batch == 1 || syb % vec == 0);
+  const int64_t cpg = gn / vec;
+  if (vec_ok && gm == 1 && cpg <= 32 && (32 % cpg) == 0) {
+    // Row groups of at most one warp (1x128 and narrower): contiguous row spans.
+    constexpr int CH = 8;
+    const int64_t spans_per_row = (n / vec + 32 * CH - 1) / (32 * CH);
+    const int64_t rows = batch * m;
+    quant::RowSpanArgs a{x, sxb, sxm, y, syb, sym, scale, ssb, ssm, ssn, m, n, rows, spans_per_row,
+                         rows * spans_per_row, eps};
+    return dispatch_xy(xt, yt, [&](auto xc, auto yc) -> int {
+      constexpr int XT = decltype(xc)::value;
+      constexpr int YT = decltype(yc)::value;
+      auto go = [&](auto kernel) -> int {
+        const int64_t warps_per_cta = quant::kThreads / 32;
+        int64_t grid = (a.units + warps_per_cta - 1) / warps_per_cta;
+        grid = std::min<int64_t>(grid, (int64_t)di.sm_count * 3);
+        kernel<<<(unsigned)grid, quant::kThreads, 0, stream>>>(a);
+        return check_launch("quant_rowspan_kernel");
+      };
+      const bool recip = mode == quant::kDeqReciprocal;
+      switch (cpg) {
+        case 1: return recip ? go(quant::quant_rowspan_kernel<XT, YT, 1, CH, quant::kDeqReciprocal>)
+                             : go(quant::quant_rowspan_kernel<XT, YT, 1, CH, quant::kDeqDivide>);
+        case 2: return recip ? go(quant::quant_rowspan_kernel<XT, YT, 2, CH, quant::kDeqReciprocal>)
+                             : go(quant::quant_rowspan_kernel<XT, YT, 2, CH, quant::kDeqDivide>);
+        case 4: return recip ? go(quant::quant_rowspan_kernel<XT, YT, 4, CH, quant::kDeqReciprocal>)
+                             : go(quant::quant_rowspan_kernel<XT, YT, 4, CH, quant::kDeqDivide>);
+        case 8: return recip ? go(quant::quant_rowspan_kernel<XT, YT, 8, CH, quant::kDeqReciprocal>)
+                             : go(quant::quant_rowspan_kernel<XT, YT, 8, CH, quant::kDeqDivide>);
+        case 16: return recip ? go(quant::quant_rowspan_kernel<XT, YT, 16, CH, quant::kDeqReciprocal>)
+                              : go(quant::quant_rowspan_kernel<XT, YT, 16, CH, quant::kDeqDivide>);
+        default: return recip ? go(quant::quant_rowspan_kernel<XT, YT, 32, CH, quant::kDeqReciprocal>)
+                              : go(quant::quant_rowspan_kernel<XT, YT, 32, CH, quant::kDeqDivide>);
+      }
+    });
+  }
   if (vec_ok) {
     quant::GroupArgs a{x, sxb, sxm, y, syb, sym, scale, ssb, ssm, ssn, batch, m, n, gm, gn, groups_m, groups_n,
                        num_groups, eps};
@@ -181,30 +216,36 @@ void ensure_smem_attr(K kernel, int bytes) {
   cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
-template <int BN, bool A_MN, bool B_MN, int FMT>
+template <int BN, bool A_MN, bool B_MN, int FMT, bool COLU>
 int launch_bmm(const CUtensorMap& ta, const CUtensorMap& tb, const gemm::Params& p, int sm_count,
                cudaStream_t stream) {
   using S = gemm::Smem<BN>;
-  auto kernel = gemm::bmm_scaled_kernel<BN, A_MN, B_MN, FMT>;
+  auto kernel = gemm::bmm_scaled_kernel<BN, A_MN, B_MN, FMT, COLU>;
   ensure_smem_attr(kernel, S::ALLOC);
   const int grid = std::min(p.num_tiles, sm_count);
   kernel<<<grid, gemm::kThreads, S::ALLOC, stream>>>(ta, tb, p);
   return check_launch("bmm_scaled_kernel");
 }
 
+template <int BN, bool A_MN, bool B_MN, int FMT>
+int launch_bmm_cols(const CUtensorMap& ta, const CUtensorMap& tb, const gemm::Params& p, int sm, cudaStream_t s) {
+  if (p.col_uniform) return launch_bmm<BN, A_MN, B_MN, FMT, true>(ta, tb, p, sm, s);
+  return launch_bmm<BN, A_MN, B_MN, FMT, false>(ta, tb, p, sm, s);
+}
+
 template <int BN>
 int dispatch_bmm_layout(bool a_mn, bool b_mn, int fmt, const CUtensorMap& ta, const CUtensorMap& tb,
                         const gemm::Params& p, int sm, cudaStream_t s) {
   if (fmt == 0) {
-    if (!a_mn && !b_mn) return launch_bmm<BN, false, false, 0>(ta, tb, p, sm, s);
-    if (!a_mn && b_mn) return launch_bmm<BN, false, true, 0>(ta, tb, p, sm, s);
-    if (a_mn && !b_mn) return launch_bmm<BN, true, false, 0>(ta, tb, p, sm, s);
-    return launch_bmm<BN, true, true, 0>(ta, tb, p, sm, s);
+    if (!a_mn && !b_mn) return launch_bmm_cols<BN, false, false, 0>(ta, tb, p, sm, s);
+    if (!a_mn && b_mn) return launch_bmm_cols<BN, false, true, 0>(ta, tb, p, sm, s);
+    if (a_mn && !b_mn) return launch_bmm_cols<BN, true, false, 0>(ta, tb, p, sm, s);
+    return launch_bmm_cols<BN, true, true, 0>(ta, tb, p, sm, s);
   }
-  if (!a_mn && !b_mn) return launch_bmm<BN, false, false, 1>(ta, tb, p, sm, s);
-  if (!a_mn && b_mn) return launch_bmm<BN, false, true, 1>(ta, tb, p, sm, s);
-  if (a_mn && !b_mn) return launch_bmm<BN, true, false, 1>(ta, tb, p, sm, s);
-  return launch_bmm<BN, true, true, 1>(ta, tb, p, sm, s);
+  if (!a_mn && !b_mn) return launch_bmm_cols<BN, false, false, 1>(ta, tb, p, sm, s);
+  if (!a_mn && b_mn) return launch_bmm_cols<BN, false, true, 1>(ta, tb, p, sm, s);
+  if (a_mn && !b_mn) return launch_bmm_cols<BN, true, false, 1>(ta, tb, p, sm, s);
+  return launch_bmm_cols<BN, true, true, 1>(ta, tb, p, sm, s);
 }
 
 // ---------------------------------------------------------------------------

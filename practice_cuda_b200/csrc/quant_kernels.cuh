@@ -34,36 +34,55 @@ struct GroupArgs {
   float eps;
 };
 
-// 16-byte chunk of input converted to VEC floats.
+// 16-byte chunk of input kept as raw bits (4 registers); converted to fp32
+// element by element when needed.
 template <int XT>
 struct Chunk {
   using T = typename InType<XT>::T;
   static constexpr int VEC = 16 / (int)sizeof(T);
-  float v[VEC];
-  __device__ __forceinline__ void load(const T* p) {
-    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p));
-    const T* e = reinterpret_cast<const T*>(&raw);
-#pragma unroll
-    for (int i = 0; i < VEC; ++i) v[i] = InType<XT>::to_f32(e[i]);
+  uint4 raw;
+  __device__ __forceinline__ void load(const T* p) { raw = __ldg(reinterpret_cast<const uint4*>(p)); }
+  __device__ __forceinline__ uint32_t word(int i) const {
+    return i == 0 ? raw.x : i == 1 ? raw.y : i == 2 ? raw.z : raw.w;
   }
+  __device__ __forceinline__ float v(int i) const {
+    if constexpr (XT == PCB_DTYPE_F32) {
+      return __uint_as_float(word(i));
+    } else if constexpr (XT == PCB_DTYPE_BF16) {
+      const uint32_t w = word(i >> 1);
+      return __uint_as_float((i & 1) ? (w & 0xffff0000u) : (w << 16));
+    } else {
+      const uint32_t w = word(i >> 1);
+      return __half2float(__ushort_as_half((unsigned short)((i & 1) ? (w >> 16) : (w & 0xffffu))));
+    }
+  }
+  // max |x| over the chunk as fp32 bits (NaN compares above +inf).
   __device__ __forceinline__ uint32_t amax_bits() const {
-    uint32_t a = 0;
-#pragma unroll
-    for (int i = 0; i < VEC; ++i) a = max(a, abs_bits(v[i]));
-    return a;
+    if constexpr (XT == PCB_DTYPE_F32) {
+      return max(max(raw.x & 0x7fffffffu, raw.y & 0x7fffffffu), max(raw.z & 0x7fffffffu, raw.w & 0x7fffffffu));
+    } else {
+      const uint32_t m2 = __vmaxu2(__vmaxu2(raw.x & 0x7fff7fffu, raw.y & 0x7fff7fffu),
+                                   __vmaxu2(raw.z & 0x7fff7fffu, raw.w & 0x7fff7fffu));
+      const uint32_t m = max(m2 & 0xffffu, m2 >> 16);
+      if constexpr (XT == PCB_DTYPE_BF16) {
+        return m << 16;
+      } else {
+        return __float_as_uint(__half2float(__ushort_as_half((unsigned short)m)));
+      }
+    }
   }
   template <int YT>
   __device__ __forceinline__ void store(uint8_t* q, float qs) const {
     if constexpr (VEC == 8) {
       uint2 out;
-      out.x = (uint32_t)cvt2_fp8<YT>(__fmul_rn(v[0], qs), __fmul_rn(v[1], qs)) |
-              ((uint32_t)cvt2_fp8<YT>(__fmul_rn(v[2], qs), __fmul_rn(v[3], qs)) << 16);
-      out.y = (uint32_t)cvt2_fp8<YT>(__fmul_rn(v[4], qs), __fmul_rn(v[5], qs)) |
-              ((uint32_t)cvt2_fp8<YT>(__fmul_rn(v[6], qs), __fmul_rn(v[7], qs)) << 16);
+      out.x = (uint32_t)cvt2_fp8<YT>(__fmul_rn(v(0), qs), __fmul_rn(v(1), qs)) |
+              ((uint32_t)cvt2_fp8<YT>(__fmul_rn(v(2), qs), __fmul_rn(v(3), qs)) << 16);
+      out.y = (uint32_t)cvt2_fp8<YT>(__fmul_rn(v(4), qs), __fmul_rn(v(5), qs)) |
+              ((uint32_t)cvt2_fp8<YT>(__fmul_rn(v(6), qs), __fmul_rn(v(7), qs)) << 16);
       *reinterpret_cast<uint2*>(q) = out;
     } else {
-      uint32_t out = (uint32_t)cvt2_fp8<YT>(__fmul_rn(v[0], qs), __fmul_rn(v[1], qs)) |
-                     ((uint32_t)cvt2_fp8<YT>(__fmul_rn(v[2], qs), __fmul_rn(v[3], qs)) << 16);
+      uint32_t out = (uint32_t)cvt2_fp8<YT>(__fmul_rn(v(0), qs), __fmul_rn(v(1), qs)) |
+                     ((uint32_t)cvt2_fp8<YT>(__fmul_rn(v(2), qs), __fmul_rn(v(3), qs)) << 16);
       *reinterpret_cast<uint32_t*>(q) = out;
     }
   }
@@ -182,6 +201,83 @@ __global__ void __launch_bounds__(kThreads) quant_groups_kernel(const GroupArgs 
   }
 }
 
+// Row groups (block_m == 1) of CPG <= 32 chunks, e.g. 1x128 tiles: each warp
+// streams a contiguous span of 32*CH chunks of one row, so every load
+// instruction covers 512 contiguous bytes and each thread keeps CH 16-byte
+// loads in flight.  Register i of lane l holds chunk i*32+l of the span,
+// which belongs to group (i*32+l)/CPG: the amax of register i reduces over
+// aligned runs of CPG lanes.
+struct RowSpanArgs {
+  const void* x;
+  int64_t sxb, sxm;
+  void* y;
+  int64_t syb, sym;
+  float* scale;
+  int64_t ssb, ssm, ssn;
+  int64_t m, n;
+  int64_t rows;           // batch * m
+  int64_t spans_per_row;
+  int64_t units;          // rows * spans_per_row
+  float eps;
+};
+
+template <int XT, int YT, int CPG, int CH, int MODE>
+__global__ void __launch_bounds__(kThreads, 3) quant_rowspan_kernel(const RowSpanArgs args) {
+  using C = Chunk<XT>;
+  using T = typename C::T;
+  constexpr int VEC = C::VEC;
+  constexpr int SPAN_CHUNKS = 32 * CH;
+  constexpr int GN = CPG * VEC;  // group width in elements
+  static_assert(CPG <= 32 && (32 % CPG) == 0, "groups must tile a warp");
+  const int lane = threadIdx.x & 31;
+  const int64_t warp_global = ((int64_t)blockIdx.x * kThreads + threadIdx.x) >> 5;
+  const int64_t warp_stride = ((int64_t)gridDim.x * kThreads) >> 5;
+  const float fp8_max = Fp8Max<YT>::value;
+  const int64_t nchunks_row = args.n / VEC;
+  for (int64_t u = warp_global; u < args.units; u += warp_stride) {
+    const int64_t row = u / args.spans_per_row;
+    const int64_t span = u - row * args.spans_per_row;
+    const int64_t bi = row / args.m, r = row - bi * args.m;
+    const T* xr = static_cast<const T*>(args.x) + bi * args.sxb + r * args.sxm;
+    uint8_t* yr = static_cast<uint8_t*>(args.y) + bi * args.syb + r * args.sym;
+    const int64_t c0 = span * SPAN_CHUNKS;
+    // Chunks of this lane: c0 + i*32 + lane for i < CH, valid while < nchunks_row.
+    const int64_t left = nchunks_row - c0 - lane;
+    const int valid = (int)(left <= 0 ? 0 : (left + 31) / 32);
+    const T* xs = xr + (c0 + lane) * VEC;
+    uint8_t* ys = yr + (c0 + lane) * VEC;
+    C reg[CH];
+    uint32_t am[CH];
+#pragma unroll
+    for (int i = 0; i < CH; ++i) {
+      am[i] = 0;
+      if (i < valid) {
+        reg[i].load(xs + i * 32 * VEC);
+        am[i] = reg[i].amax_bits();
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < CH; ++i) {
+#pragma unroll
+      for (int off = CPG / 2; off > 0; off >>= 1) am[i] = max(am[i], __shfl_xor_sync(0xffffffffu, am[i], off));
+    }
+    float* srow = args.scale + bi * args.ssb + r * args.ssm;
+    const int64_t g0 = ((c0 + lane) * VEC) / GN;  // group of register 0
+#pragma unroll
+    for (int i = 0; i < CH; ++i) {
+      if (i < valid) {
+        const float safe = clamp_min_eps(__uint_as_float(am[i]), args.eps);
+        const float qs = quant_scale_from_amax(safe, fp8_max);
+        reg[i].template store<YT>(ys + i * 32 * VEC, qs);
+        if ((lane % CPG) == 0) {
+          const float deq = (MODE == kDeqReciprocal) ? __frcp_rn(qs) : __fdiv_rn(safe, fp8_max);
+          srow[(g0 + i * (32 * VEC / GN)) * args.ssn] = deq;
+        }
+      }
+    }
+  }
+}
+
 // Generic fallback: one CTA per group, scalar strided loads, two passes.
 struct GenericArgs {
   const void* x;
@@ -287,7 +383,7 @@ __global__ void __launch_bounds__(kThreads) quant_cols_cluster_kernel(const ColA
       C ch;
       ch.load(xb + r * args.sxm + col);
 #pragma unroll
-      for (int i = 0; i < VEC; ++i) am[i] = max(am[i], abs_bits(ch.v[i]));
+      for (int i = 0; i < VEC; ++i) am[i] = max(am[i], abs_bits(ch.v(i)));
     }
   }
 #pragma unroll
@@ -317,8 +413,8 @@ __global__ void __launch_bounds__(kThreads) quant_cols_cluster_kernel(const ColA
       uint8_t out[VEC];
 #pragma unroll
       for (int i = 0; i < VEC; i += 2) {
-        const uint16_t p = cvt2_fp8<YT>(__fmul_rn(ch.v[i], qs_s[cc * VEC + i]),
-                                        __fmul_rn(ch.v[i + 1], qs_s[cc * VEC + i + 1]));
+        const uint16_t p = cvt2_fp8<YT>(__fmul_rn(ch.v(i), qs_s[cc * VEC + i]),
+                                        __fmul_rn(ch.v(i + 1), qs_s[cc * VEC + i + 1]));
         out[i] = (uint8_t)(p & 0xff);
         out[i + 1] = (uint8_t)(p >> 8);
       }
