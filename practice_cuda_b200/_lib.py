@@ -12,7 +12,8 @@ import threading
 
 import torch
 
-LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libpcb200.so")
+# PCB200_LIB points at another build of the same library (profiling variants only).
+LIB_PATH = os.environ.get("PCB200_LIB") or os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libpcb200.so")
 
 PCB_OK = 0
 PCB_ERR_INVALID = 1

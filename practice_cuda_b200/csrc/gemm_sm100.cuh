@@ -24,6 +24,14 @@ constexpr int UMMA_K = 32;        // K per tcgen05.mma for 8-bit inputs
 constexpr int kThreads = 384;
 constexpr int kEpiWarp0 = 4;
 constexpr int kEpiThreads = 256;
+// Register split for the 128x256 tile (setmaxnreg): the producer/MMA
+// warpgroup drops to kLowRegs so the epilogue warpgroups can hold 128 fp32
+// accumulators per thread.  The launch holds kThreads * kLaunchRegs registers
+// (checked on the host before every launch) and the split adds up to it.
+constexpr int kLaunchRegs = 168;  // 65536 / 384, rounded down to a multiple of 8
+constexpr int kLowRegs = 40;
+constexpr int kHighRegs = 232;
+static_assert(128 * kLowRegs + 256 * kHighRegs == kThreads * kLaunchRegs, "register split must match the launch");
 constexpr int kNumAcc = 4;        // TMEM accumulator buffers of BN fp32 columns
 constexpr int kScalePrefetch = 4;  // K groups of scales kept in flight per epilogue thread
 
@@ -51,6 +59,7 @@ struct Params {
   int bias_dtype;
   int activation;
   int inject_error;
+  int debug_flags;  // profiling only: 1 = epilogue skips its math, 2 = no MMAs issued
 };
 
 // ---------------------------------------------------------------------------
@@ -111,6 +120,16 @@ __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[3
       : "r"(taddr));
 }
 
+// 16 consecutive fp32 columns of this thread's TMEM lane (no wait).
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // UMMA shared-memory descriptor for a 128-byte-swizzled tile.
@@ -164,8 +183,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   using S = Smem<BN>;
   constexpr int STAGES = S::STAGES;
   constexpr int EPI_COLS = S::EPI_COLS;
-  constexpr uint32_t TMEM_COLS = kNumAcc * BN;
-  static_assert(kNumAcc * BN <= 512, "TMEM holds 512 fp32 columns");
+  constexpr int NACC = (BN == 256) ? 2 : kNumAcc;
+  constexpr uint32_t TMEM_COLS = NACC * BN;
+  static_assert(NACC * BN <= 512, "TMEM holds 512 fp32 columns");
   constexpr uint32_t IDESC = make_idesc(BN, AB_FMT, A_MN ? 1 : 0, B_MN ? 1 : 0);
   constexpr uint32_t STAGE_TX = S::A_BYTES + S::B_BYTES;
 
@@ -174,8 +194,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t s_base = smem_u32(smem);
   const uint32_t bar_full = s_base + S::OFF_BAR;                  // [STAGES]
   const uint32_t bar_empty = bar_full + 8 * STAGES;               // [STAGES]
-  const uint32_t bar_tfull = bar_empty + 8 * STAGES;              // [kNumAcc]
-  const uint32_t bar_tempty = bar_tfull + 8 * kNumAcc;            // [kNumAcc]
+  const uint32_t bar_tfull = bar_empty + 8 * STAGES;              // [NACC]
+  const uint32_t bar_tempty = bar_tfull + 8 * kNumAcc;            // [NACC]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 4);
 
@@ -187,7 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar_full + 8 * s, 1);
       mbar_init(bar_empty + 8 * s, 1);
     }
-    for (int i = 0; i < kNumAcc; ++i) {
+    for (int i = 0; i < NACC; ++i) {
       mbar_init(bar_tfull + 8 * i, 1);
       mbar_init(bar_tempty + 8 * i, 8);  // one arrive per epilogue warp
     }
@@ -207,6 +227,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int tiles_per_batch = p.m_blocks * p.n_blocks;
 
+  if (warp < 4) {
+    if constexpr (BN == 256) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kLowRegs));
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
     if (lane == 0) {
@@ -258,8 +280,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
         for (int g = 0; g < p.num_groups && ok; ++g) {
-          const uint32_t abuf = acc_cnt % kNumAcc;
-          const uint32_t aphase = (acc_cnt / kNumAcc) & 1;
+          const uint32_t abuf = acc_cnt % NACC;
+          const uint32_t aphase = (acc_cnt / NACC) & 1;
           if (!mbar_wait_bounded(bar_tempty + 8 * abuf, aphase ^ 1, abort_flag, SITE_GEMM_MMA)) {
             ok = false;
             break;
@@ -284,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               // 32 rows of 128 bytes for an MN-major tile (encoded >> 4).
               const uint64_t a_off = A_MN ? (uint64_t)(kk * UMMA_K * 128 >> 4) : (uint64_t)(kk * UMMA_K >> 4);
               const uint64_t b_off = B_MN ? (uint64_t)(kk * UMMA_K * 128 >> 4) : (uint64_t)(kk * UMMA_K >> 4);
-              umma_f8(d_tmem, adesc0 + a_off, bdesc0 + b_off, IDESC, (ks > ks0 || kk > 0) ? 1u : 0u);
+              if (!(p.debug_flags & 2)) umma_f8(d_tmem, adesc0 + a_off, bdesc0 + b_off, IDESC, (ks > ks0 || kk > 0) ? 1u : 0u);
             }
             umma_commit(bar_empty + 8 * stage);  // smem stage free once these MMAs retire
             if (++stage == STAGES) {
@@ -298,8 +320,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp >= kEpiWarp0) {
+  }
+  } else {
     // -------------------------------- epilogue --------------------------------
+    if constexpr (BN == 256) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kHighRegs));
     const int ew = warp - kEpiWarp0;        // 0..7
     const int quarter = warp & 3;           // TMEM lane quarter
     const int half = ew >> 2;               // column half
@@ -343,8 +367,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < kScalePrefetch; ++j) {
           const int g = g0 + j;
           if (g >= p.num_groups || !ok) break;
-          const uint32_t abuf = acc_cnt % kNumAcc;
-          const uint32_t aphase = (acc_cnt / kNumAcc) & 1;
+          const uint32_t abuf = acc_cnt % NACC;
+          const uint32_t aphase = (acc_cnt / NACC) & 1;
           const float s_row = rs[j];
           const float s_col = cs[j];
           if (g + kScalePrefetch < p.num_groups) {
@@ -366,33 +390,57 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
+          if (p.debug_flags & 1) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_tempty + 8 * abuf);
+            ++acc_cnt;
+            continue;
+          }
           const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN + half * EPI_COLS;
-          uint32_t v[EPI_COLS / 32][32];
+          if constexpr (EPI_COLS <= 64) {
+            // Narrow half-tile: load it all, free the buffer, then FMA.
+            uint32_t v[EPI_COLS / 32][32];
 #pragma unroll
-          for (int c = 0; c < EPI_COLS / 32; ++c) tmem_ld32_nowait(taddr + c * 32, v[c]);
-          tmem_wait_ld();
-          // The accumulator buffer is free as soon as it sits in registers.
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar_tempty + 8 * abuf);
-          if constexpr (COL_UNIFORM) {
-            const float s = s_row * s_col;
-            const float2 s2 = make_float2(s, s);
-#pragma unroll
-            for (int c = 0; c < EPI_COLS / 32; ++c)
-#pragma unroll
-              for (int i = 0; i < 16; ++i)
-                acc[c * 16 + i] = __ffma2_rn(make_float2(__uint_as_float(v[c][2 * i]), __uint_as_float(v[c][2 * i + 1])),
-                                             s2, acc[c * 16 + i]);
-          } else {
+            for (int c = 0; c < EPI_COLS / 32; ++c) tmem_ld32_nowait(taddr + c * 32, v[c]);
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_tempty + 8 * abuf);
 #pragma unroll
             for (int c = 0; c < EPI_COLS / 32; ++c)
 #pragma unroll
               for (int i = 0; i < 16; ++i) {
-                const float2 s2 = make_float2(s_row * colscale[c * 32 + 2 * i], s_row * colscale[c * 32 + 2 * i + 1]);
+                float2 s2;
+                if constexpr (COL_UNIFORM) {
+                  s2 = make_float2(s_row * s_col, s_row * s_col);
+                } else {
+                  s2 = make_float2(s_row * colscale[c * 32 + 2 * i], s_row * colscale[c * 32 + 2 * i + 1]);
+                }
                 acc[c * 16 + i] = __ffma2_rn(make_float2(__uint_as_float(v[c][2 * i]), __uint_as_float(v[c][2 * i + 1])),
                                              s2, acc[c * 16 + i]);
               }
+          } else {
+            // Wide half-tile: 16 columns at a time keeps the registers in budget.
+#pragma unroll
+            for (int c = 0; c < EPI_COLS / 16; ++c) {
+              uint32_t v[16];
+              tmem_ld16_nowait(taddr + c * 16, v);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                float2 s2;
+                if constexpr (COL_UNIFORM) {
+                  s2 = make_float2(s_row * s_col, s_row * s_col);
+                } else {
+                  s2 = make_float2(s_row * colscale[c * 16 + 2 * i], s_row * colscale[c * 16 + 2 * i + 1]);
+                }
+                acc[c * 8 + i] = __ffma2_rn(make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])), s2,
+                                            acc[c * 8 + i]);
+              }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_tempty + 8 * abuf);
           }
           ++acc_cnt;
         }

@@ -4,6 +4,7 @@
 
 #include <atomic>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -221,6 +222,18 @@ int launch_bmm(const CUtensorMap& ta, const CUtensorMap& tb, const gemm::Params&
                cudaStream_t stream) {
   using S = gemm::Smem<BN>;
   auto kernel = gemm::bmm_scaled_kernel<BN, A_MN, B_MN, FMT, COLU>;
+  if constexpr (BN == 256) {
+    // This instantiation re-splits its registers with setmaxnreg; the split
+    // is only valid when the launch holds exactly kLaunchRegs per thread
+    // (otherwise setmaxnreg.inc could never be satisfied), so never launch a
+    // build where ptxas chose another count.
+    static const int num_regs = [&] {
+      cudaFuncAttributes fa{};
+      return cudaFuncGetAttributes(&fa, kernel) == cudaSuccess ? fa.numRegs : -1;
+    }();
+    if (num_regs != gemm::kLaunchRegs)
+      return fail(PCB_ERR_UNSUPPORTED, "bmm kernel register count differs from its setmaxnreg split");
+  }
   ensure_smem_attr(kernel, S::ALLOC);
   const int grid = std::min(p.num_tiles, sm_count);
   kernel<<<grid, gemm::kThreads, S::ALLOC, stream>>>(ta, tb, p);
@@ -511,7 +524,9 @@ int pcb_bmm_scaled(const void* a, int64_t sab, int64_t sam, int64_t sak, const v
   // Operand layouts (bytes == elements for fp8).
   bool a_mn = false, b_mn = false;
   CUtensorMap ta, tb;
-  const int bn = 128;  // see below
+  // 128x256 tiles (128x128 when N <= 128): 32 KB of fp8 operands per
+  // 128-deep K stage feed 8.4 MFLOP, which keeps L2 traffic per FLOP low.
+  const int bn = (n > 128) ? 256 : 128;
   if (k == 0) {
     // No K stages: the kernel only writes bias/zeros; the maps are never read.
     std::memset(&ta, 0, sizeof(ta));
@@ -546,8 +561,7 @@ int pcb_bmm_scaled(const void* a, int64_t sab, int64_t sam, int64_t sak, const v
                                 (uint32_t)bn);
   if (!okA || !okB) return fail(PCB_ERR_LAYOUT, "cuTensorMapEncodeTiled rejected the operand layout");
   }
-  // 128x128 tiles: two epilogue warpgroups hold 64 fp32 accumulators per
-  // thread without spilling (a 128x256 tile would need 128 per thread).
+  // Each epilogue thread holds BN/2 fp32 accumulators of its row.
   const int epi_cols = bn / 2;
 
   gemm::Params p{};
@@ -585,8 +599,12 @@ int pcb_bmm_scaled(const void* a, int64_t sab, int64_t sam, int64_t sak, const v
   p.bias_dtype = bias_dtype;
   p.activation = activation;
   p.inject_error = g_inject_error.exchange(0);
+  // Profiling knob (never set in production): PCB200_BMM_DEBUG=1 skips the
+  // epilogue math, =2 skips the MMAs; results are then meaningless.
+  if (const char* dbg = std::getenv("PCB200_BMM_DEBUG")) p.debug_flags = std::atoi(dbg);
   const int fmt = (ab_dtype == PCB_DTYPE_E4M3) ? 0 : 1;
   cudaStream_t s = (cudaStream_t)stream;
+  if (bn == 256) return dispatch_bmm_layout<256>(a_mn, b_mn, fmt, ta, tb, p, di.sm_count, s);
   return dispatch_bmm_layout<128>(a_mn, b_mn, fmt, ta, tb, p, di.sm_count, s);
 }
 
