@@ -107,6 +107,70 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
                : "memory");
 }
 
+
+// ---- CTA-pair (cta_group::2) helpers -------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared-memory offset in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// TMA load into this CTA's shared memory that completes its bytes on the
+// pair leader's mbarrier (`bar_cluster` is a shared::cluster address).
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar_cluster, int c0,
+                                                 int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+      "%5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// M=256 MMA over the CTA pair: A rows and B columns split between the two
+// CTAs' shared memory at the same offsets; issued by the leader only.
+__device__ __forceinline__ void umma_f8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on `bar` in both CTAs of the pair once the leader's MMAs retire.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"((uint16_t)0x3)
+      : "memory");
+}
+
 // 32 consecutive fp32 columns of this thread's TMEM lane (no wait).
 __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
@@ -147,16 +211,18 @@ __device__ __forceinline__ uint64_t make_sw128_desc(uint32_t saddr, uint32_t lbo
 }
 
 // Instruction descriptor: fp32 accumulate, fp8 A/B, M=128, N=BN.
-__host__ __device__ constexpr uint32_t make_idesc(int bn, int ab_fmt, int a_mn, int b_mn) {
+__host__ __device__ constexpr uint32_t make_idesc(int bn, int ab_fmt, int a_mn, int b_mn, int m = BM) {
   return (1u << 4) | ((uint32_t)ab_fmt << 7) | ((uint32_t)ab_fmt << 10) | ((uint32_t)a_mn << 15) |
-         ((uint32_t)b_mn << 16) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+         ((uint32_t)b_mn << 16) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
-template <int BN>
+template <int BN, bool PAIR = false>
 struct Smem {
-  static constexpr int STAGES = (BN == 256) ? 4 : 6;
-  static constexpr int A_BYTES = BM * BK;  // 16 KB
-  static constexpr int B_BYTES = BN * BK;  // 32 / 16 KB
+  // A CTA pair splits the B tile: each CTA stages BN/2 of its N rows.
+  static constexpr int B_ROWS = PAIR ? BN / 2 : BN;
+  static constexpr int STAGES = (BN == 256 && !PAIR) ? 4 : 6;
+  static constexpr int A_BYTES = BM * BK;      // 16 KB
+  static constexpr int B_BYTES = B_ROWS * BK;  // 32 / 16 KB
   static constexpr int EPI_COLS = BN / 2;
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
@@ -176,18 +242,21 @@ __device__ __forceinline__ float load_bias(const void* p, int dt, long long off)
   return __half2float(static_cast<const __half*>(p)[off]);
 }
 
-template <int BN, bool A_MN, bool B_MN, int AB_FMT, bool COL_UNIFORM>
+template <int BN, bool A_MN, bool B_MN, int AB_FMT, bool COL_UNIFORM, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     bmm_scaled_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                       const Params p) {
-  using S = Smem<BN>;
+  static_assert(!PAIR || BN == 256, "the CTA pair runs 256x256 tiles");
+  using S = Smem<BN, PAIR>;
   constexpr int STAGES = S::STAGES;
   constexpr int EPI_COLS = S::EPI_COLS;
   constexpr int NACC = (BN == 256) ? 2 : kNumAcc;
   constexpr uint32_t TMEM_COLS = NACC * BN;
   static_assert(NACC * BN <= 512, "TMEM holds 512 fp32 columns");
-  constexpr uint32_t IDESC = make_idesc(BN, AB_FMT, A_MN ? 1 : 0, B_MN ? 1 : 0);
-  constexpr uint32_t STAGE_TX = S::A_BYTES + S::B_BYTES;
+  constexpr uint32_t IDESC = make_idesc(BN, AB_FMT, A_MN ? 1 : 0, B_MN ? 1 : 0, PAIR ? 2 * BM : BM);
+  // Bytes that land on the (leader's) full barrier per stage.
+  constexpr uint32_t STAGE_TX = (PAIR ? 2 : 1) * (S::A_BYTES + S::B_BYTES);
+  constexpr int TILE_M = PAIR ? 2 * BM : BM;  // output rows per tile
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -201,6 +270,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // Pair mode: cluster of two CTAs; rank 0 (leader) issues the MMAs and owns
+  // the full / tmem-empty barriers that both CTAs feed.
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int first_tile = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int tile_step = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -209,16 +284,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < NACC; ++i) {
       mbar_init(bar_tfull + 8 * i, 1);
-      mbar_init(bar_tempty + 8 * i, 8);  // one arrive per epilogue warp
+      mbar_init(bar_tempty + 8 * i, PAIR ? 16 : 8);  // one arrive per epilogue warp (of both CTAs)
     }
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tmap(&tmap_a);
     prefetch_tmap(&tmap_b);
   }
-  if (warp == 1) tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
-  tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) {
+    if (warp == 1) tmem_alloc_pair(smem_u32(tmem_slot), TMEM_COLS);
+    tc_fence_before();
+    cluster_sync_all();  // both CTAs' barriers exist before any remote arrive / TMA
+  } else {
+    if (warp == 1) tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+  }
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -235,30 +316,42 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      for (int tile = first_tile; tile < p.num_tiles && ok; tile += tile_step) {
         const int b = tile / tiles_per_batch;
         const int rem = tile - b * tiles_per_batch;
         const int mb = rem / p.n_blocks;
         const int nb = rem - mb * p.n_blocks;
+        const int a_row = mb * TILE_M + (int)rank * BM;           // this CTA's A rows
+        const int b_col = nb * BN + (int)rank * S::B_ROWS;        // this CTA's B columns
         for (int ks = 0; ks < p.k_stages; ++ks) {
           if (!mbar_wait_bounded(bar_empty + 8 * stage, phase ^ 1, abort_flag, SITE_GEMM_PRODUCER)) {
             ok = false;
             break;
           }
           const uint32_t fb = bar_full + 8 * stage;
-          mbar_arrive_expect_tx(fb, STAGE_TX);
           const uint32_t sa_dst = s_base + S::OFF_A + stage * S::A_BYTES;
           const uint32_t sb_dst = s_base + S::OFF_B + stage * S::B_BYTES;
-          if constexpr (A_MN) {
-            tma_load_3d(sa_dst, &tmap_a, fb, mb * BM, ks * BK, b);
+          if constexpr (PAIR) {
+            if (leader) mbar_arrive_expect_tx(fb, STAGE_TX);
+            const uint32_t fbl = mapa_shared(fb, 0);
+            if constexpr (A_MN) tma_load_3d_pair(sa_dst, &tmap_a, fbl, a_row, ks * BK, b);
+            else tma_load_3d_pair(sa_dst, &tmap_a, fbl, ks * BK, a_row, b);
+            if constexpr (B_MN) tma_load_3d_pair(sb_dst, &tmap_b, fbl, b_col, ks * BK, b);
+            else tma_load_3d_pair(sb_dst, &tmap_b, fbl, ks * BK, b_col, b);
           } else {
-            tma_load_3d(sa_dst, &tmap_a, fb, ks * BK, mb * BM, b);
-          }
-          if constexpr (B_MN) {
+            mbar_arrive_expect_tx(fb, STAGE_TX);
+            if constexpr (A_MN) {
+              tma_load_3d(sa_dst, &tmap_a, fb, a_row, ks * BK, b);
+            } else {
+              tma_load_3d(sa_dst, &tmap_a, fb, ks * BK, a_row, b);
+            }
+            if constexpr (B_MN) {
 #pragma unroll
-            for (int j = 0; j < BN / 128; ++j) tma_load_3d(sb_dst + j * 128 * BK, &tmap_b, fb, nb * BN + j * 128, ks * BK, b);
-          } else {
-            tma_load_3d(sb_dst, &tmap_b, fb, ks * BK, nb * BN, b);
+              for (int j = 0; j < BN / 128; ++j)
+                tma_load_3d(sb_dst + j * 128 * BK, &tmap_b, fb, b_col + j * 128, ks * BK, b);
+            } else {
+              tma_load_3d(sb_dst, &tmap_b, fb, ks * BK, b_col, b);
+            }
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -273,12 +366,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------- MMA issuer -------------------------------
-    if (lane == 0) {
+    if (lane == 0 && leader) {
       int stage = 0;
       uint32_t phase = 0;
       uint32_t acc_cnt = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      for (int tile = first_tile; tile < p.num_tiles && ok; tile += tile_step) {
         for (int g = 0; g < p.num_groups && ok; ++g) {
           const uint32_t abuf = acc_cnt % NACC;
           const uint32_t aphase = (acc_cnt / NACC) & 1;
@@ -306,16 +399,23 @@ __global__ void __launch_bounds__(kThreads, 1)
               // 32 rows of 128 bytes for an MN-major tile (encoded >> 4).
               const uint64_t a_off = A_MN ? (uint64_t)(kk * UMMA_K * 128 >> 4) : (uint64_t)(kk * UMMA_K >> 4);
               const uint64_t b_off = B_MN ? (uint64_t)(kk * UMMA_K * 128 >> 4) : (uint64_t)(kk * UMMA_K >> 4);
-              if (!(p.debug_flags & 2)) umma_f8(d_tmem, adesc0 + a_off, bdesc0 + b_off, IDESC, (ks > ks0 || kk > 0) ? 1u : 0u);
+              if (!(p.debug_flags & 2)) {
+                if constexpr (PAIR) umma_f8_pair(d_tmem, adesc0 + a_off, bdesc0 + b_off, IDESC, (ks > ks0 || kk > 0) ? 1u : 0u);
+                else umma_f8(d_tmem, adesc0 + a_off, bdesc0 + b_off, IDESC, (ks > ks0 || kk > 0) ? 1u : 0u);
+              }
             }
-            umma_commit(bar_empty + 8 * stage);  // smem stage free once these MMAs retire
+            // smem stage (of both CTAs) free once these MMAs retire
+            if constexpr (PAIR) umma_commit_pair(bar_empty + 8 * stage);
+            else umma_commit(bar_empty + 8 * stage);
             if (++stage == STAGES) {
               stage = 0;
               phase ^= 1;
             }
           }
           if (!ok) break;
-          umma_commit(bar_tfull + 8 * abuf);  // accumulator of group g ready
+          // accumulator of group g ready (in both CTAs' TMEM)
+          if constexpr (PAIR) umma_commit_pair(bar_tfull + 8 * abuf);
+          else umma_commit(bar_tfull + 8 * abuf);
           ++acc_cnt;
         }
       }
@@ -331,12 +431,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* colscale = reinterpret_cast<float*>(smem + S::OFF_COLSCALE) + ew * EPI_COLS;
     uint32_t acc_cnt = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+    // The tmem-empty barrier lives in the leader; the follower arrives remotely.
+    const uint32_t bar_tempty_l = PAIR ? mapa_shared(bar_tempty, 0) : bar_tempty;
+    for (int tile = first_tile; tile < p.num_tiles && ok; tile += tile_step) {
       const int b = tile / tiles_per_batch;
       const int rem = tile - b * tiles_per_batch;
       const int mb = rem / p.n_blocks;
       const int nb = rem - mb * p.n_blocks;
-      const int row = mb * BM + row_in_tile;
+      const int row = mb * TILE_M + (int)rank * BM + row_in_tile;
       const int col0 = nb * BN + half * EPI_COLS;
       const bool row_ok = row < p.m;
       const float* sa_row = p.sa ? p.sa + (long long)b * p.ssab + (long long)(row / p.qbm) * p.ssam : nullptr;
@@ -392,7 +494,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           if (p.debug_flags & 1) {
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar_tempty + 8 * abuf);
+            if (lane == 0) {
+              if constexpr (PAIR) mbar_arrive_cluster(bar_tempty_l + 8 * abuf);
+              else mbar_arrive(bar_tempty + 8 * abuf);
+            }
             ++acc_cnt;
             continue;
           }
@@ -405,7 +510,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_wait_ld();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar_tempty + 8 * abuf);
+            if (lane == 0) {
+              if constexpr (PAIR) mbar_arrive_cluster(bar_tempty_l + 8 * abuf);
+              else mbar_arrive(bar_tempty + 8 * abuf);
+            }
 #pragma unroll
             for (int c = 0; c < EPI_COLS / 32; ++c)
 #pragma unroll
@@ -440,7 +548,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar_tempty + 8 * abuf);
+            if (lane == 0) {
+              if constexpr (PAIR) mbar_arrive_cluster(bar_tempty_l + 8 * abuf);
+              else mbar_arrive(bar_tempty + 8 * abuf);
+            }
           }
           ++acc_cnt;
         }
@@ -521,9 +632,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+  if constexpr (PAIR) {
+    cluster_sync_all();  // no CTA leaves while its peer may still touch its smem / barriers
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  } else {
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+  }
 }
 
 }  // namespace gemm

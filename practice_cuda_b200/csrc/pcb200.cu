@@ -217,11 +217,11 @@ void ensure_smem_attr(K kernel, int bytes) {
   cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
-template <int BN, bool A_MN, bool B_MN, int FMT, bool COLU>
+template <int BN, bool A_MN, bool B_MN, int FMT, bool COLU, bool PAIR>
 int launch_bmm(const CUtensorMap& ta, const CUtensorMap& tb, const gemm::Params& p, int sm_count,
                cudaStream_t stream) {
-  using S = gemm::Smem<BN>;
-  auto kernel = gemm::bmm_scaled_kernel<BN, A_MN, B_MN, FMT, COLU>;
+  using S = gemm::Smem<BN, PAIR>;
+  auto kernel = gemm::bmm_scaled_kernel<BN, A_MN, B_MN, FMT, COLU, PAIR>;
   if constexpr (BN == 256) {
     // This instantiation re-splits its registers with setmaxnreg; the split
     // is only valid when the launch holds exactly kLaunchRegs per thread
@@ -235,30 +235,48 @@ int launch_bmm(const CUtensorMap& ta, const CUtensorMap& tb, const gemm::Params&
       return fail(PCB_ERR_UNSUPPORTED, "bmm kernel register count differs from its setmaxnreg split");
   }
   ensure_smem_attr(kernel, S::ALLOC);
-  const int grid = std::min(p.num_tiles, sm_count);
-  kernel<<<grid, gemm::kThreads, S::ALLOC, stream>>>(ta, tb, p);
+  if constexpr (PAIR) {
+    // Clusters of two CTAs (one tile of 256 rows each), one CTA per SM.
+    const int clusters = std::min(p.num_tiles, sm_count / 2);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(2 * clusters), 1, 1);
+    cfg.blockDim = dim3(gemm::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = S::ALLOC;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kernel, ta, tb, p);
+  } else {
+    const int grid = std::min(p.num_tiles, sm_count);
+    kernel<<<grid, gemm::kThreads, S::ALLOC, stream>>>(ta, tb, p);
+  }
   return check_launch("bmm_scaled_kernel");
 }
 
-template <int BN, bool A_MN, bool B_MN, int FMT>
+template <int BN, bool A_MN, bool B_MN, int FMT, bool PAIR>
 int launch_bmm_cols(const CUtensorMap& ta, const CUtensorMap& tb, const gemm::Params& p, int sm, cudaStream_t s) {
-  if (p.col_uniform) return launch_bmm<BN, A_MN, B_MN, FMT, true>(ta, tb, p, sm, s);
-  return launch_bmm<BN, A_MN, B_MN, FMT, false>(ta, tb, p, sm, s);
+  if (p.col_uniform) return launch_bmm<BN, A_MN, B_MN, FMT, true, PAIR>(ta, tb, p, sm, s);
+  return launch_bmm<BN, A_MN, B_MN, FMT, false, PAIR>(ta, tb, p, sm, s);
 }
 
-template <int BN>
+template <int BN, bool PAIR>
 int dispatch_bmm_layout(bool a_mn, bool b_mn, int fmt, const CUtensorMap& ta, const CUtensorMap& tb,
                         const gemm::Params& p, int sm, cudaStream_t s) {
   if (fmt == 0) {
-    if (!a_mn && !b_mn) return launch_bmm_cols<BN, false, false, 0>(ta, tb, p, sm, s);
-    if (!a_mn && b_mn) return launch_bmm_cols<BN, false, true, 0>(ta, tb, p, sm, s);
-    if (a_mn && !b_mn) return launch_bmm_cols<BN, true, false, 0>(ta, tb, p, sm, s);
-    return launch_bmm_cols<BN, true, true, 0>(ta, tb, p, sm, s);
+    if (!a_mn && !b_mn) return launch_bmm_cols<BN, false, false, 0, PAIR>(ta, tb, p, sm, s);
+    if (!a_mn && b_mn) return launch_bmm_cols<BN, false, true, 0, PAIR>(ta, tb, p, sm, s);
+    if (a_mn && !b_mn) return launch_bmm_cols<BN, true, false, 0, PAIR>(ta, tb, p, sm, s);
+    return launch_bmm_cols<BN, true, true, 0, PAIR>(ta, tb, p, sm, s);
   }
-  if (!a_mn && !b_mn) return launch_bmm_cols<BN, false, false, 1>(ta, tb, p, sm, s);
-  if (!a_mn && b_mn) return launch_bmm_cols<BN, false, true, 1>(ta, tb, p, sm, s);
-  if (a_mn && !b_mn) return launch_bmm_cols<BN, true, false, 1>(ta, tb, p, sm, s);
-  return launch_bmm_cols<BN, true, true, 1>(ta, tb, p, sm, s);
+  if (!a_mn && !b_mn) return launch_bmm_cols<BN, false, false, 1, PAIR>(ta, tb, p, sm, s);
+  if (!a_mn && b_mn) return launch_bmm_cols<BN, false, true, 1, PAIR>(ta, tb, p, sm, s);
+  if (a_mn && !b_mn) return launch_bmm_cols<BN, true, false, 1, PAIR>(ta, tb, p, sm, s);
+  return launch_bmm_cols<BN, true, true, 1, PAIR>(ta, tb, p, sm, s);
 }
 
 // ---------------------------------------------------------------------------
@@ -527,6 +545,11 @@ int pcb_bmm_scaled(const void* a, int64_t sab, int64_t sam, int64_t sak, const v
   // 128x256 tiles (128x128 when N <= 128): 32 KB of fp8 operands per
   // 128-deep K stage feed 8.4 MFLOP, which keeps L2 traffic per FLOP low.
   const int bn = (n > 128) ? 256 : 128;
+  // 256x256 tiles on a CTA pair (cta_group::2) once M spans two 128-row halves:
+  // each CTA stages its own 128 A rows and half of the B tile, halving the
+  // B traffic per SM.  PCB200_BMM_PAIR=0 turns it off (profiling knob).
+  bool pair = bn == 256 && m > 128;
+  if (const char* e = std::getenv("PCB200_BMM_PAIR")) pair = pair && std::atoi(e) != 0;
   if (k == 0) {
     // No K stages: the kernel only writes bias/zeros; the maps are never read.
     std::memset(&ta, 0, sizeof(ta));
@@ -558,7 +581,7 @@ int pcb_bmm_scaled(const void* a, int64_t sab, int64_t sam, int64_t sak, const v
                   : make_map_u8(&ta, a, kk, (uint64_t)m, (uint64_t)batch, (uint64_t)sam, (uint64_t)sab, 128);
   bool okB = b_mn ? make_map_u8(&tb, b, (uint64_t)n, kk, (uint64_t)batch, (uint64_t)sbk, (uint64_t)sbb, 128)
                   : make_map_u8(&tb, b, kk, (uint64_t)n, (uint64_t)batch, (uint64_t)sbn, (uint64_t)sbb,
-                                (uint32_t)bn);
+                                (uint32_t)(pair ? bn / 2 : bn));
   if (!okA || !okB) return fail(PCB_ERR_LAYOUT, "cuTensorMapEncodeTiled rejected the operand layout");
   }
   // Each epilogue thread holds BN/2 fp32 accumulators of its row.
@@ -569,7 +592,8 @@ int pcb_bmm_scaled(const void* a, int64_t sab, int64_t sam, int64_t sak, const v
   p.m = (int)m;
   p.n = (int)n;
   p.k = (int)k;
-  p.m_blocks = (int)((m + gemm::BM - 1) / gemm::BM);
+  const int tile_m = pair ? 2 * gemm::BM : gemm::BM;
+  p.m_blocks = (int)((m + tile_m - 1) / tile_m);
   p.n_blocks = (int)((n + bn - 1) / bn);
   p.num_tiles = (int)(batch * p.m_blocks * p.n_blocks);
   p.k_stages = (int)k_stages;
@@ -604,8 +628,9 @@ int pcb_bmm_scaled(const void* a, int64_t sab, int64_t sam, int64_t sak, const v
   if (const char* dbg = std::getenv("PCB200_BMM_DEBUG")) p.debug_flags = std::atoi(dbg);
   const int fmt = (ab_dtype == PCB_DTYPE_E4M3) ? 0 : 1;
   cudaStream_t s = (cudaStream_t)stream;
-  if (bn == 256) return dispatch_bmm_layout<256>(a_mn, b_mn, fmt, ta, tb, p, di.sm_count, s);
-  return dispatch_bmm_layout<128>(a_mn, b_mn, fmt, ta, tb, p, di.sm_count, s);
+  if (pair) return dispatch_bmm_layout<256, true>(a_mn, b_mn, fmt, ta, tb, p, di.sm_count, s);
+  if (bn == 256) return dispatch_bmm_layout<256, false>(a_mn, b_mn, fmt, ta, tb, p, di.sm_count, s);
+  return dispatch_bmm_layout<128, false>(a_mn, b_mn, fmt, ta, tb, p, di.sm_count, s);
 }
 
 }  // extern "C"
