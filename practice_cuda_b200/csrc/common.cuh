@@ -82,6 +82,35 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait that polls with the non-blocking test_wait (no suspend): used
+// where the arrival comes from the other CTA of a pair.
+__device__ __forceinline__ bool mbar_spin_bounded(uint32_t bar, uint32_t parity, volatile int* abort_flag, int site) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if ((i & 255u) == 0u) {
+      if (*abort_flag) return false;
+      if (global_timer_ns() - t0 > kWaitLimitNs) break;
+    }
+  }
+  report_error(PCB_ERR_TIMEOUT, site);
+  *abort_flag = 1;
+  return false;
+}
+
 // Bounded wait on phase `parity` of an mbarrier.  Returns false (after
 // recording an error and raising the CTA abort flag) when the wait runs out
 // or when another warp of the CTA already aborted.

@@ -59,7 +59,7 @@ struct Params {
   int bias_dtype;
   int activation;
   int inject_error;
-  int debug_flags;  // profiling only: 1 = epilogue skips its math, 2 = no MMAs issued
+  int debug_flags;  // profiling only: 1 = epilogue skips its math, 2 = no MMAs issued, 4 = MMA ignores tmem-empty
 };
 
 // ---------------------------------------------------------------------------
@@ -275,6 +275,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
   const bool leader = rank == 0;
   const int first_tile = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  // Waits whose arrival may come from the peer CTA poll without suspending
+  // (flag 16 switches back to the suspending try_wait, profiling only).
+  const bool spin = PAIR && !(p.debug_flags & 16);
+  auto wait = [&](uint32_t bar, uint32_t parity, int site) -> bool {
+    return spin ? mbar_spin_bounded(bar, parity, abort_flag, site) : mbar_wait_bounded(bar, parity, abort_flag, site);
+  };
   const int tile_step = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
   if (threadIdx.x == 0) {
@@ -324,7 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int a_row = mb * TILE_M + (int)rank * BM;           // this CTA's A rows
         const int b_col = nb * BN + (int)rank * S::B_ROWS;        // this CTA's B columns
         for (int ks = 0; ks < p.k_stages; ++ks) {
-          if (!mbar_wait_bounded(bar_empty + 8 * stage, phase ^ 1, abort_flag, SITE_GEMM_PRODUCER)) {
+          if (!wait(bar_empty + 8 * stage, phase ^ 1, SITE_GEMM_PRODUCER)) {
             ok = false;
             break;
           }
@@ -375,7 +381,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int g = 0; g < p.num_groups && ok; ++g) {
           const uint32_t abuf = acc_cnt % NACC;
           const uint32_t aphase = (acc_cnt / NACC) & 1;
-          if (!mbar_wait_bounded(bar_tempty + 8 * abuf, aphase ^ 1, abort_flag, SITE_GEMM_MMA)) {
+          if (!(p.debug_flags & 4) && !wait(bar_tempty + 8 * abuf, aphase ^ 1, SITE_GEMM_MMA)) {
             ok = false;
             break;
           }
@@ -384,7 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int ks0 = g * p.stages_per_group;
           const int ks1 = min(p.k_stages, ks0 + p.stages_per_group);
           for (int ks = ks0; ks < ks1; ++ks) {
-            if (!mbar_wait_bounded(bar_full + 8 * stage, phase, abort_flag, SITE_GEMM_MMA)) {
+            if (!wait(bar_full + 8 * stage, phase, SITE_GEMM_MMA)) {
               ok = false;
               break;
             }
@@ -487,7 +493,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             __syncwarp();
           }
-          if (!mbar_wait_bounded(bar_tfull + 8 * abuf, aphase, abort_flag, SITE_GEMM_EPILOGUE)) {
+          if (!wait(bar_tfull + 8 * abuf, aphase, SITE_GEMM_EPILOGUE)) {
             ok = false;
             break;
           }

@@ -545,11 +545,18 @@ int pcb_bmm_scaled(const void* a, int64_t sab, int64_t sam, int64_t sak, const v
   // 128x256 tiles (128x128 when N <= 128): 32 KB of fp8 operands per
   // 128-deep K stage feed 8.4 MFLOP, which keeps L2 traffic per FLOP low.
   const int bn = (n > 128) ? 256 : 128;
-  // 256x256 tiles on a CTA pair (cta_group::2) once M spans two 128-row halves:
-  // each CTA stages its own 128 A rows and half of the B tile, halving the
-  // B traffic per SM.  PCB200_BMM_PAIR=0 turns it off (profiling knob).
-  bool pair = bn == 256 && m > 128;
-  if (const char* e = std::getenv("PCB200_BMM_PAIR")) pair = pair && std::atoi(e) != 0;
+  // 256x256 tiles on a CTA pair (cta_group::2) when M spans two 128-row
+  // halves and the tile has a single K group (per-channel / per-tensor): each
+  // CTA stages its own 128 A rows and half of the B tile.  With per-block
+  // scales every K group is a TMEM round trip between the leader's MMA and
+  // both CTAs' epilogues, which costs more across the pair than the smaller
+  // B traffic saves, so those stay on one CTA.  PCB200_BMM_PAIR=0 turns the
+  // pair off, =2 forces it on for per-block too (profiling knobs).
+  bool pair = bn == 256 && m > 128 && qbk >= k;
+  if (const char* e = std::getenv("PCB200_BMM_PAIR")) {
+    const int v = std::atoi(e);
+    pair = (v == 2) ? (bn == 256 && m > 128) : (pair && v != 0);
+  }
   if (k == 0) {
     // No K stages: the kernel only writes bias/zeros; the maps are never read.
     std::memset(&ta, 0, sizeof(ta));

@@ -234,3 +234,18 @@ def test_zero_k_and_empty():
     bias = torch.randn((2, 64, 32), device=DEV)
     out = get_bmm("b200_per_channel_a_k_b_n").fn(qa, qb, bias=bias, out_dtype=torch.float32)
     assert torch.equal(out, bias)
+
+
+@pytest.mark.parametrize("layout", ["a_k_b_n", "a_k_b_k", "a_m_b_n"])
+def test_per_block_on_cta_pair(layout, monkeypatch):
+    """Per-block scales on the 256x256 CTA-pair kernel (selected by default only
+    for single-K-group tiles; forced here so both kernels stay covered)."""
+    monkeypatch.setenv("PCB200_BMM_PAIR", "2")
+    B, M, K, N = 2, 384, 640, 512
+    a = synthetic((B, M, K), outliers=True, seed=40)
+    b = synthetic((B, K, N), std=0.02, seed=41)
+    qa, qb, ablk, bblk = _quant_pair("1x128_128x128", a, b)
+    ref = _promoted_ref(qa, qb, ablk, bblk)
+    qa2, qb2 = _operands_for_layout(qa, qb, layout)
+    out = get_bmm(f"b200_per_block_1x128_128x128_{layout}").fn(qa2, qb2)
+    assert_bmm_close(out, ref, f"pair {layout}")
