@@ -183,6 +183,29 @@ int pcb_bmm_scaled(const void* a, int64_t sab, int64_t sam, int64_t sak,
                    int activation, void* stream);
 
 /*
+ * Fused quantize -> scaled FP8 GEMM (BASELINE cfg4).  The reference's fused
+ * kernel (kernels/fp8_bmm/kernel/fp8_quant_bmm_fused_kernel.py:39-146) does not
+ * run (SURVEY: produce_quant_scale is called with one argument and returns
+ * nothing); this is the working equivalent of what it intended:
+ *   A = per-block 1x128 quantization of x (bf16/fp16, K contiguous) with the
+ *       arithmetic of pcb_quant_per_block, done inside the GEMM;
+ *   C[b] = act(sum_g (A_g B_g) * a_scale(b,m,g) * sb(b,g,n) + bias)
+ * with 128-deep K groups and sb as in pcb_bmm_scaled (B e4m3, K- or N-major).
+ * Optional outputs: xq (fp8 [B,M,K], K contiguous, row stride sxqm) and xs
+ * (fp32 [B,M,ceil(K/128)]) receive the quantized activation and its scales,
+ * bit-identical to pcb_quant_per_block (NULL to skip).  K % 8 == 0.
+ */
+int pcb_quant_bmm_fused(const void* x, int x_dtype, int64_t sxb, int64_t sxm, int64_t sxk,
+                        const void* b, int64_t sbb, int64_t sbk, int64_t sbn, int b_dtype,
+                        int64_t batch, int64_t m, int64_t n, int64_t k,
+                        const float* scale_b, int64_t ssbb, int64_t ssbk, int64_t ssbn, int64_t qbn,
+                        const void* bias, int bias_dtype, int64_t sbib, int64_t sbim, int64_t sbin,
+                        void* c, int c_dtype, int64_t scb, int64_t scm, int64_t scn,
+                        void* xq, int64_t sxqb, int64_t sxqm,
+                        float* xs, int64_t sxsb, int64_t sxsm, int64_t sxsk,
+                        int activation, float eps, void* stream);
+
+/*
  * Byte repack: dst[b, r, c] = src[b*ssb + r*ssr + c*ssc] for c < cols and 0
  * for cols <= c < cols_padded.  Used by the host shims to turn an fp8 operand
  * whose strides do not fit TMA into a K-major, 16-byte aligned copy -- the

@@ -75,6 +75,18 @@ _SIGNATURES = {
          _vp, _i, _i64, _i64, _i64,  # c
          _i, _vp],
     ),
+    "pcb_quant_bmm_fused": (
+        _i,
+        [_vp, _i, _i64, _i64, _i64,  # x
+         _vp, _i64, _i64, _i64, _i,  # b
+         _i64, _i64, _i64, _i64,  # batch m n k
+         _vp, _i64, _i64, _i64, _i64,  # scale b, strides, qbn
+         _vp, _i, _i64, _i64, _i64,  # bias
+         _vp, _i, _i64, _i64, _i64,  # c
+         _vp, _i64, _i64,  # xq
+         _vp, _i64, _i64, _i64,  # xs
+         _i, _f, _vp],
+    ),
     "pcb_pack_u8": (_i, [_vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp]),
 }
 

@@ -59,6 +59,13 @@ struct Params {
   int bias_dtype;
   int activation;
   int inject_error;
+  // Fused quantize->GEMM only: optional copies of the quantized activation
+  // (fp8 [B, M, K], K contiguous) and its 1x128 scales [B, M, ceil(K/128)].
+  void* xq;
+  long long sxqb, sxqm;
+  float* xs;
+  long long sxsb, sxsm, sxsk;
+  float eps;
   int debug_flags;  // profiling only: 1 = epilogue skips its math, 2 = no MMAs issued, 4 = MMA ignores tmem-empty
 };
 
@@ -240,6 +247,80 @@ __device__ __forceinline__ float load_bias(const void* p, int dt, long long off)
   if (dt == PCB_DTYPE_F32) return __ldg(static_cast<const float*>(p) + off);
   if (dt == PCB_DTYPE_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[off]);
   return __half2float(static_cast<const __half*>(p)[off]);
+}
+
+// Bias, activation, cast and store of one thread's EPI_COLS accumulators
+// (row `row`, columns [col0, col0 + EPI_COLS)) of batch `b`.
+template <int EPI_COLS>
+__device__ __forceinline__ void store_row(const Params& p, float* accf, int b, int row, int col0) {
+  if (row < p.m) {
+    const long long crow = (long long)b * p.scb + (long long)row * p.scm;
+    if (p.bias) {
+#pragma unroll
+      for (int i = 0; i < EPI_COLS; ++i) {
+        const int c = col0 + i;
+        if (c < p.n)
+          accf[i] += load_bias(p.bias, p.bias_dtype, (long long)b * p.sbib + (long long)row * p.sbim + (long long)c * p.sbin);
+      }
+    }
+    if (p.activation == PCB_ACT_GELU) {
+#pragma unroll
+      for (int i = 0; i < EPI_COLS; ++i) accf[i] = gelu_erf(accf[i]);
+    }
+    const bool full = p.c_vec && (col0 + EPI_COLS <= p.n);
+    if (p.c_dtype == PCB_DTYPE_BF16 || p.c_dtype == PCB_DTYPE_F16) {
+      uint16_t* out = static_cast<uint16_t*>(p.c) + crow + col0;
+      if (full) {
+#pragma unroll
+        for (int i = 0; i < EPI_COLS; i += 8) {
+          uint4 w;
+          uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            if (p.c_dtype == PCB_DTYPE_BF16) {
+              __nv_bfloat162 h = __floats2bfloat162_rn(accf[i + 2 * q], accf[i + 2 * q + 1]);
+              wp[q] = *reinterpret_cast<uint32_t*>(&h);
+            } else {
+              __half2 h = __floats2half2_rn(accf[i + 2 * q], accf[i + 2 * q + 1]);
+              wp[q] = *reinterpret_cast<uint32_t*>(&h);
+            }
+          }
+          *reinterpret_cast<uint4*>(out + i) = w;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < EPI_COLS; ++i) {
+          if (col0 + i < p.n) {
+            if (p.c_dtype == PCB_DTYPE_BF16) {
+              __nv_bfloat16 h = __float2bfloat16_rn(accf[i]);
+              out[i] = *reinterpret_cast<uint16_t*>(&h);
+            } else {
+              __half h = __float2half_rn(accf[i]);
+              out[i] = *reinterpret_cast<uint16_t*>(&h);
+            }
+          }
+        }
+      }
+    } else if (p.c_dtype == PCB_DTYPE_F32) {
+      float* out = static_cast<float*>(p.c) + crow + col0;
+      if (full) {
+#pragma unroll
+        for (int i = 0; i < EPI_COLS; i += 4)
+          *reinterpret_cast<float4*>(out + i) = make_float4(accf[i], accf[i + 1], accf[i + 2], accf[i + 3]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < EPI_COLS; ++i)
+          if (col0 + i < p.n) out[i] = accf[i];
+      }
+    } else {
+      uint8_t* out = static_cast<uint8_t*>(p.c) + crow + col0;
+#pragma unroll
+      for (int i = 0; i < EPI_COLS; ++i) {
+        if (col0 + i < p.n)
+          out[i] = (p.c_dtype == PCB_DTYPE_E4M3) ? cvt1_fp8<PCB_DTYPE_E4M3>(accf[i]) : cvt1_fp8<PCB_DTYPE_E5M2>(accf[i]);
+      }
+    }
+  }
 }
 
 template <int BN, bool A_MN, bool B_MN, int AB_FMT, bool COL_UNIFORM, bool PAIR>
@@ -566,74 +647,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       // Bias, activation, cast, store.
       float* accf = reinterpret_cast<float*>(acc);
-      if (row_ok) {
-        const long long crow = (long long)b * p.scb + (long long)row * p.scm;
-        if (p.bias) {
-#pragma unroll
-          for (int i = 0; i < EPI_COLS; ++i) {
-            const int c = col0 + i;
-            if (c < p.n)
-              accf[i] += load_bias(p.bias, p.bias_dtype, (long long)b * p.sbib + (long long)row * p.sbim + (long long)c * p.sbin);
-          }
-        }
-        if (p.activation == PCB_ACT_GELU) {
-#pragma unroll
-          for (int i = 0; i < EPI_COLS; ++i) accf[i] = gelu_erf(accf[i]);
-        }
-        const bool full = p.c_vec && (col0 + EPI_COLS <= p.n);
-        if (p.c_dtype == PCB_DTYPE_BF16 || p.c_dtype == PCB_DTYPE_F16) {
-          uint16_t* out = static_cast<uint16_t*>(p.c) + crow + col0;
-          if (full) {
-#pragma unroll
-            for (int i = 0; i < EPI_COLS; i += 8) {
-              uint4 w;
-              uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                if (p.c_dtype == PCB_DTYPE_BF16) {
-                  __nv_bfloat162 h = __floats2bfloat162_rn(accf[i + 2 * q], accf[i + 2 * q + 1]);
-                  wp[q] = *reinterpret_cast<uint32_t*>(&h);
-                } else {
-                  __half2 h = __floats2half2_rn(accf[i + 2 * q], accf[i + 2 * q + 1]);
-                  wp[q] = *reinterpret_cast<uint32_t*>(&h);
-                }
-              }
-              *reinterpret_cast<uint4*>(out + i) = w;
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < EPI_COLS; ++i) {
-              if (col0 + i < p.n) {
-                if (p.c_dtype == PCB_DTYPE_BF16) {
-                  __nv_bfloat16 h = __float2bfloat16_rn(accf[i]);
-                  out[i] = *reinterpret_cast<uint16_t*>(&h);
-                } else {
-                  __half h = __float2half_rn(accf[i]);
-                  out[i] = *reinterpret_cast<uint16_t*>(&h);
-                }
-              }
-            }
-          }
-        } else if (p.c_dtype == PCB_DTYPE_F32) {
-          float* out = static_cast<float*>(p.c) + crow + col0;
-          if (full) {
-#pragma unroll
-            for (int i = 0; i < EPI_COLS; i += 4)
-              *reinterpret_cast<float4*>(out + i) = make_float4(accf[i], accf[i + 1], accf[i + 2], accf[i + 3]);
-          } else {
-#pragma unroll
-            for (int i = 0; i < EPI_COLS; ++i)
-              if (col0 + i < p.n) out[i] = accf[i];
-          }
-        } else {
-          uint8_t* out = static_cast<uint8_t*>(p.c) + crow + col0;
-#pragma unroll
-          for (int i = 0; i < EPI_COLS; ++i) {
-            if (col0 + i < p.n)
-              out[i] = (p.c_dtype == PCB_DTYPE_E4M3) ? cvt1_fp8<PCB_DTYPE_E4M3>(accf[i]) : cvt1_fp8<PCB_DTYPE_E5M2>(accf[i]);
-          }
-        }
-      }
+      store_row<EPI_COLS>(p, accf, b, row, col0);
     }
   }
 

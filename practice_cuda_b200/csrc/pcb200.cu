@@ -12,6 +12,7 @@
 #include "common.cuh"
 #include "gemm_sm100.cuh"
 #include "quant_kernels.cuh"
+#include "gemm_fused_sm100.cuh"
 
 using namespace pcb;
 
@@ -216,6 +217,35 @@ void ensure_smem_attr(K kernel, int bytes) {
   // and keeps this stateless across devices and threads.
   cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
+
+// 3-D map of 16-bit elements (inner, outer, batch), unswizzled box (128, 128, 1):
+// one 128x128 activation tile with 256-byte rows.
+bool make_map_x16(CUtensorMap* map, const void* base, int dt, uint64_t inner, uint64_t outer, uint64_t batch,
+                  uint64_t outer_stride_bytes, uint64_t batch_stride_bytes) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {inner, outer, batch};
+  if (batch <= 1) batch_stride_bytes = std::max<uint64_t>(16, ((outer * outer_stride_bytes + 15) / 16) * 16);
+  cuuint64_t strides[2] = {outer_stride_bytes, batch_stride_bytes};
+  cuuint32_t box[3] = {128, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapDataType t =
+      dt == PCB_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return fn(map, t, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <bool B_MN, int XT, bool COLU>
+int launch_fused(const CUtensorMap& tx, const CUtensorMap& tb, const gemm::Params& p, int sm_count,
+                 cudaStream_t stream) {
+  auto kernel = gemm::quant_bmm_fused_kernel<B_MN, XT, COLU>;
+  ensure_smem_attr(kernel, gemm::FusedSmem::ALLOC);
+  const int grid = std::min(p.num_tiles, sm_count);
+  kernel<<<grid, gemm::kFusedThreads, gemm::FusedSmem::ALLOC, stream>>>(tx, tb, p);
+  return check_launch("quant_bmm_fused_kernel");
+}
+
 
 template <int BN, bool A_MN, bool B_MN, int FMT, bool COLU, bool PAIR>
 int launch_bmm(const CUtensorMap& ta, const CUtensorMap& tb, const gemm::Params& p, int sm_count,
@@ -494,6 +524,101 @@ int pcb_quant_per_tensor_noalloc(const void* x, int x_dtype, int64_t batch, int6
     quant::tensor_cast_kernel<XT, YT><<<cast_grid, quant::kThreads, 0, s>>>(a);
     return check_launch("tensor_cast_kernel (noalloc)");
   });
+}
+
+int pcb_quant_bmm_fused(const void* x, int x_dtype, int64_t sxb, int64_t sxm, int64_t sxk, const void* b,
+                        int64_t sbb, int64_t sbk, int64_t sbn, int b_dtype, int64_t batch, int64_t m, int64_t n,
+                        int64_t k, const float* scale_b, int64_t ssbb, int64_t ssbk, int64_t ssbn, int64_t qbn,
+                        const void* bias, int bias_dtype, int64_t sbib, int64_t sbim, int64_t sbin, void* c,
+                        int c_dtype, int64_t scb, int64_t scm, int64_t scn, void* xq, int64_t sxqb, int64_t sxqm,
+                        float* xs, int64_t sxsb, int64_t sxsm, int64_t sxsk, int activation, float eps,
+                        void* stream) {
+  if (batch < 0 || m < 0 || n < 0 || k < 0) return fail(PCB_ERR_INVALID, "negative size");
+  if (x_dtype != PCB_DTYPE_BF16 && x_dtype != PCB_DTYPE_F16) return fail(PCB_ERR_INVALID, "x must be BF16 or F16");
+  if (b_dtype != PCB_DTYPE_E4M3) return fail(PCB_ERR_INVALID, "B must be E4M3");
+  if (elem_size(c_dtype) == 0) return fail(PCB_ERR_INVALID, "bad output dtype");
+  if (bias && !is_float_in(bias_dtype)) return fail(PCB_ERR_INVALID, "bias dtype must be F32/F16/BF16");
+  if (activation != PCB_ACT_NONE && activation != PCB_ACT_GELU) return fail(PCB_ERR_INVALID, "bad activation");
+  if (qbn <= 0) return fail(PCB_ERR_INVALID, "qbn must be positive");
+  if (batch == 0 || m == 0 || n == 0) return PCB_OK;
+  if (k == 0) return fail(PCB_ERR_UNSUPPORTED, "K must be positive for the fused path");
+  if (!x || !b || !c) return fail(PCB_ERR_INVALID, "null pointer");
+  if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX || batch > 65535)
+    return fail(PCB_ERR_UNSUPPORTED, "dimension too large");
+  if (scn != 1) return fail(PCB_ERR_LAYOUT, "output must be contiguous along N");
+  if (sxk != 1 || (sxm * 2) % 16 != 0 || (batch > 1 && (sxb * 2) % 16 != 0) || !aligned(x, 16) || k % 8 != 0)
+    return fail(PCB_ERR_LAYOUT, "x must be K-contiguous with 16-byte aligned rows");
+  if (xq && (sxqm % 8 != 0 || !aligned(xq, 8))) return fail(PCB_ERR_LAYOUT, "quantized x output rows must be 8-byte aligned");
+  const DeviceInfo di = device_info();
+  if (di.major != 10) return fail(PCB_ERR_DEVICE, "pcb_quant_bmm_fused needs an sm_100 device");
+  bool b_mn;
+  if (sbk == 1) {
+    b_mn = false;
+    if (sbn % 16 != 0) return fail(PCB_ERR_LAYOUT, "K-major B stride must be a multiple of 16 bytes");
+  } else if (sbn == 1) {
+    b_mn = true;
+    if (sbk % 16 != 0) return fail(PCB_ERR_LAYOUT, "N-major B stride must be a multiple of 16 bytes");
+  } else {
+    return fail(PCB_ERR_LAYOUT, "B must be contiguous along K or N");
+  }
+  if ((batch > 1 && sbb % 16 != 0) || !aligned(b, 16)) return fail(PCB_ERR_LAYOUT, "B batch stride / base alignment");
+  CUtensorMap tx, tb;
+  if (!make_map_x16(&tx, x, x_dtype, (uint64_t)k, (uint64_t)m, (uint64_t)batch, (uint64_t)sxm * 2,
+                    (uint64_t)sxb * 2))
+    return fail(PCB_ERR_LAYOUT, "cuTensorMapEncodeTiled rejected x");
+  const bool okB = b_mn ? make_map_u8(&tb, b, (uint64_t)n, (uint64_t)k, (uint64_t)batch, (uint64_t)sbk, (uint64_t)sbb, 128)
+                        : make_map_u8(&tb, b, (uint64_t)k, (uint64_t)n, (uint64_t)batch, (uint64_t)sbn, (uint64_t)sbb, 128);
+  if (!okB) return fail(PCB_ERR_LAYOUT, "cuTensorMapEncodeTiled rejected B");
+  constexpr int bn = gemm::FusedSmem::BN;
+  gemm::Params p{};
+  p.batch = (int)batch;
+  p.m = (int)m;
+  p.n = (int)n;
+  p.k = (int)k;
+  p.m_blocks = (int)((m + gemm::BM - 1) / gemm::BM);
+  p.n_blocks = (int)((n + bn - 1) / bn);
+  p.num_tiles = (int)(batch * p.m_blocks * p.n_blocks);
+  p.k_stages = (int)((k + gemm::BK - 1) / gemm::BK);
+  p.stages_per_group = 1;
+  p.num_groups = p.k_stages;
+  p.sb = scale_b;
+  p.ssbb = ssbb;
+  p.ssbk = ssbk;
+  p.ssbn = ssbn;
+  p.qbn = (int)std::min<int64_t>(qbn, INT32_MAX);
+  p.col_uniform = (!scale_b || ssbn == 0 || qbn % gemm::FusedSmem::EPI_COLS == 0 || qbn >= n) ? 1 : 0;
+  p.c = c;
+  p.scb = scb;
+  p.scm = scm;
+  const int ces = elem_size(c_dtype);
+  p.c_dtype = c_dtype;
+  p.c_vec = (aligned(c, 16) && (scm * ces) % 16 == 0 && (batch == 1 || (scb * ces) % 16 == 0)) ? 1 : 0;
+  p.bias = bias;
+  p.sbib = sbib;
+  p.sbim = sbim;
+  p.sbin = sbin;
+  p.bias_dtype = bias_dtype;
+  p.activation = activation;
+  p.xq = xq;
+  p.sxqb = sxqb;
+  p.sxqm = sxqm;
+  p.xs = xs;
+  p.sxsb = sxsb;
+  p.sxsm = sxsm;
+  p.sxsk = sxsk;
+  p.eps = eps;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int sm = di.sm_count;
+  if (x_dtype == PCB_DTYPE_BF16) {
+    if (b_mn) return p.col_uniform ? launch_fused<true, PCB_DTYPE_BF16, true>(tx, tb, p, sm, s)
+                                   : launch_fused<true, PCB_DTYPE_BF16, false>(tx, tb, p, sm, s);
+    return p.col_uniform ? launch_fused<false, PCB_DTYPE_BF16, true>(tx, tb, p, sm, s)
+                         : launch_fused<false, PCB_DTYPE_BF16, false>(tx, tb, p, sm, s);
+  }
+  if (b_mn) return p.col_uniform ? launch_fused<true, PCB_DTYPE_F16, true>(tx, tb, p, sm, s)
+                                 : launch_fused<true, PCB_DTYPE_F16, false>(tx, tb, p, sm, s);
+  return p.col_uniform ? launch_fused<false, PCB_DTYPE_F16, true>(tx, tb, p, sm, s)
+                       : launch_fused<false, PCB_DTYPE_F16, false>(tx, tb, p, sm, s);
 }
 
 int pcb_pack_u8(const void* src, int64_t batch, int64_t rows, int64_t cols, int64_t ssb, int64_t ssr, int64_t ssc,
