@@ -17,6 +17,7 @@ from typing import Optional
 import torch
 
 from . import _lib
+from .impls._common import pack_k_major
 from .registry import QuantResult
 
 
@@ -73,10 +74,10 @@ def quant_bmm_fused(
     if return_quantized:
         xq = torch.empty((batch, m, k), device=x.device, dtype=torch.float8_e4m3fn)
         xs = torch.empty((batch, m, (k + 127) // 128), device=x.device, dtype=torch.float32)
-    bt = b.tensor
     lib = _lib.lib()
-    _lib.check(
-        lib.pcb_quant_bmm_fused(
+
+    def launch(bt):
+        return lib.pcb_quant_bmm_fused(
             x.data_ptr(), _lib.dtype_code(x.dtype), *x.stride(),
             bt.data_ptr(), *bt.stride(), _lib.dtype_code(bt.dtype),
             batch, m, n, k,
@@ -88,9 +89,12 @@ def quant_bmm_fused(
             xq.data_ptr() if xq is not None else None, *(xq.stride()[:2] if xq is not None else (0, 0)),
             xs.data_ptr() if xs is not None else None, *(xs.stride() if xs is not None else (0, 0, 0)),
             _lib.PCB_ACT[activation], eps, _lib.stream_ptr(x.device),
-        ),
-        "pcb_quant_bmm_fused",
-    )
+        )
+
+    status = launch(b.tensor)
+    if status == _lib.PCB_ERR_LAYOUT:  # B strides TMA cannot address: K-major, 16-byte padded copy
+        status = launch(pack_k_major(b.tensor, k_dim_last=False))
+    _lib.check(status, "pcb_quant_bmm_fused")
     if squeeze:
         out = out[0]
     if not return_quantized:
