@@ -301,15 +301,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           const float s_row = ring[slot * BM + row_in_tile];
           tc_fence_after();
           const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN + half * EPI_COLS;
-          uint32_t v[EPI_COLS / 32][32];
 #pragma unroll
-          for (int c = 0; c < EPI_COLS / 32; ++c) tmem_ld32_nowait(taddr + c * 32, v[c]);
-          tmem_wait_ld();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar_tempty + 8 * abuf);
-#pragma unroll
-          for (int c = 0; c < EPI_COLS / 32; ++c)
+          for (int c = 0; c < EPI_COLS / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld32_nowait(taddr + c * 32, v);
+            tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               float2 s2;
@@ -318,9 +314,13 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
               } else {
                 s2 = make_float2(s_row * colscale[c * 32 + 2 * i], s_row * colscale[c * 32 + 2 * i + 1]);
               }
-              acc[c * 16 + i] = __ffma2_rn(make_float2(__uint_as_float(v[c][2 * i]), __uint_as_float(v[c][2 * i + 1])),
-                                           s2, acc[c * 16 + i]);
+              acc[c * 16 + i] =
+                  __ffma2_rn(make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])), s2, acc[c * 16 + i]);
             }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar_tempty + 8 * abuf);
           ++acc_cnt;
         }
       }
