@@ -28,7 +28,8 @@ namespace gemm {
 constexpr int kFusedThreads = 512;
 constexpr int kFusedQuantWarp0 = 4;
 constexpr int kFusedEpiWarp0 = 8;
-constexpr int kScaleRing = 8;  // >= STAGES + kNumAcc + 1 groups in flight
+constexpr int kScaleRing = 8;
+constexpr int kFusedPrefetch = 2;  // K groups of column scales in flight per epilogue thread  // >= STAGES + kNumAcc + 1 groups in flight
 
 struct FusedSmem {
   static constexpr int BN = 128;
@@ -264,65 +265,56 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       float2 acc[EPI_COLS / 2];
 #pragma unroll
       for (int i = 0; i < EPI_COLS / 2; ++i) acc[i] = make_float2(0.f, 0.f);
-      // Column scales of the next kScalePrefetch groups stay in flight in
-      // registers (loop unrolled by kScalePrefetch: static ring indices).
       auto col_scale = [&](int g) -> float {
         return (COL_UNIFORM && sb_b && col0 < p.n)
                    ? __ldg(sb_b + (long long)g * p.ssbk + (long long)(col0 / p.qbn) * p.ssbn)
                    : 1.f;
       };
-      float cs[kScalePrefetch];
-#pragma unroll
-      for (int j = 0; j < kScalePrefetch; ++j) cs[j] = (j < p.num_groups) ? col_scale(j) : 1.f;
-      for (int g0 = 0; g0 < p.num_groups && ok; g0 += kScalePrefetch) {
-#pragma unroll
-        for (int j = 0; j < kScalePrefetch; ++j) {
-          const int g = g0 + j;
-          if (g >= p.num_groups || !ok) break;
-          const uint32_t abuf = acc_cnt % NACC;
-          const uint32_t aphase = (acc_cnt / NACC) & 1;
-          const float s_col = cs[j];
-          if (g + kScalePrefetch < p.num_groups) cs[j] = col_scale(g + kScalePrefetch);
-          if constexpr (!COL_UNIFORM) {
-            __syncwarp();
-            for (int i = lane; i < EPI_COLS; i += 32) {
-              const int c = col0 + i;
-              colscale[i] =
-                  (sb_b && c < p.n) ? __ldg(sb_b + (long long)g * p.ssbk + (long long)(c / p.qbn) * p.ssbn) : 1.f;
-            }
-            __syncwarp();
-          }
-          const uint32_t slot = acc_cnt % kScaleRing;
-          if (!mbar_wait_bounded(bar_ring + 8 * slot, (acc_cnt / kScaleRing) & 1, abort_flag, SITE_FUSED_EPILOGUE) ||
-              !mbar_wait_bounded(bar_tfull + 8 * abuf, aphase, abort_flag, SITE_FUSED_EPILOGUE)) {
-            ok = false;
-            break;
-          }
-          const float s_row = ring[slot * BM + row_in_tile];
-          tc_fence_after();
-          const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN + half * EPI_COLS;
-#pragma unroll
-          for (int c = 0; c < EPI_COLS / 32; ++c) {
-            uint32_t v[32];
-            tmem_ld32_nowait(taddr + c * 32, v);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              float2 s2;
-              if constexpr (COL_UNIFORM) {
-                s2 = make_float2(s_row * s_col, s_row * s_col);
-              } else {
-                s2 = make_float2(s_row * colscale[c * 32 + 2 * i], s_row * colscale[c * 32 + 2 * i + 1]);
-              }
-              acc[c * 16 + i] =
-                  __ffma2_rn(make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])), s2, acc[c * 16 + i]);
-            }
-          }
-          tc_fence_before();
+      float s_col_next = col_scale(0);
+      for (int g = 0; g < p.num_groups && ok; ++g) {
+        const uint32_t abuf = acc_cnt % NACC;
+        const uint32_t aphase = (acc_cnt / NACC) & 1;
+        const float s_col = s_col_next;
+        if (g + 1 < p.num_groups) s_col_next = col_scale(g + 1);  // one group ahead
+        if constexpr (!COL_UNIFORM) {
           __syncwarp();
-          if (lane == 0) mbar_arrive(bar_tempty + 8 * abuf);
-          ++acc_cnt;
+          for (int i = lane; i < EPI_COLS; i += 32) {
+            const int c = col0 + i;
+            colscale[i] =
+                (sb_b && c < p.n) ? __ldg(sb_b + (long long)g * p.ssbk + (long long)(c / p.qbn) * p.ssbn) : 1.f;
+          }
+          __syncwarp();
         }
+        const uint32_t slot = acc_cnt % kScaleRing;
+        if (!mbar_wait_bounded(bar_ring + 8 * slot, (acc_cnt / kScaleRing) & 1, abort_flag, SITE_FUSED_EPILOGUE) ||
+            !mbar_wait_bounded(bar_tfull + 8 * abuf, aphase, abort_flag, SITE_FUSED_EPILOGUE)) {
+          ok = false;
+          break;
+        }
+        const float s_row = ring[slot * BM + row_in_tile];
+        tc_fence_after();
+        const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN + half * EPI_COLS;
+#pragma unroll
+        for (int c = 0; c < EPI_COLS / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32_nowait(taddr + c * 32, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float2 s2;
+            if constexpr (COL_UNIFORM) {
+              s2 = make_float2(s_row * s_col, s_row * s_col);
+            } else {
+              s2 = make_float2(s_row * colscale[c * 32 + 2 * i], s_row * colscale[c * 32 + 2 * i + 1]);
+            }
+            acc[c * 16 + i] =
+                __ffma2_rn(make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])), s2, acc[c * 16 + i]);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_tempty + 8 * abuf);
+        ++acc_cnt;
       }
       if (!ok) break;
       store_row<EPI_COLS>(p, reinterpret_cast<float*>(acc), b, row, col0);
