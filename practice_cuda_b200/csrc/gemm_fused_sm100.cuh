@@ -205,23 +205,37 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         uint8_t* aq = smem + S::OFF_A + stage * S::A_BYTES;
         float* slot = ring + (gq % kScaleRing) * BM;
         const int kcol = ks * BK + c16 * 8;
-#pragma unroll 4
+        // All 16 row-pair loads first (explicit shared-memory loads), then the
+        // reductions and casts, so the loads overlap instead of serialising.
+        const uint32_t xs_s = smem_u32(xs) + (uint32_t)(qw * 32 + half) * 256u + (uint32_t)c16 * 16u;
+        const uint32_t aq_s = smem_u32(aq);
+        C ch[16];
+#pragma unroll
+        for (int it = 0; it < 16; ++it) {
+          asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(ch[it].raw.x), "=r"(ch[it].raw.y), "=r"(ch[it].raw.z), "=r"(ch[it].raw.w)
+                       : "r"(xs_s + (uint32_t)it * 512u));
+        }
+        uint32_t am[16];
+#pragma unroll
+        for (int it = 0; it < 16; ++it) am[it] = ch[it].amax_bits();
+#pragma unroll
+        for (int off = 8; off > 0; off >>= 1)
+#pragma unroll
+          for (int it = 0; it < 16; ++it) am[it] = max(am[it], __shfl_xor_sync(0xffffffffu, am[it], off));
+#pragma unroll
         for (int it = 0; it < 16; ++it) {
           const int r = qw * 32 + 2 * it + half;
-          C ch;
-          ch.raw = *reinterpret_cast<const uint4*>(xs + r * 256 + c16 * 16);
-          uint32_t am = ch.amax_bits();
-#pragma unroll
-          for (int off = 8; off > 0; off >>= 1) am = max(am, __shfl_xor_sync(0xffffffffu, am, off));
-          const float safe = clamp_min_eps(__uint_as_float(am), p.eps);
+          const float safe = clamp_min_eps(__uint_as_float(am[it]), p.eps);
           const float qs = quant_scale_from_amax(safe, fp8_max);
           uint2 q;
-          q.x = (uint32_t)cvt2_fp8<PCB_DTYPE_E4M3>(__fmul_rn(ch.v(0), qs), __fmul_rn(ch.v(1), qs)) |
-                ((uint32_t)cvt2_fp8<PCB_DTYPE_E4M3>(__fmul_rn(ch.v(2), qs), __fmul_rn(ch.v(3), qs)) << 16);
-          q.y = (uint32_t)cvt2_fp8<PCB_DTYPE_E4M3>(__fmul_rn(ch.v(4), qs), __fmul_rn(ch.v(5), qs)) |
-                ((uint32_t)cvt2_fp8<PCB_DTYPE_E4M3>(__fmul_rn(ch.v(6), qs), __fmul_rn(ch.v(7), qs)) << 16);
+          q.x = (uint32_t)cvt2_fp8<PCB_DTYPE_E4M3>(__fmul_rn(ch[it].v(0), qs), __fmul_rn(ch[it].v(1), qs)) |
+                ((uint32_t)cvt2_fp8<PCB_DTYPE_E4M3>(__fmul_rn(ch[it].v(2), qs), __fmul_rn(ch[it].v(3), qs)) << 16);
+          q.y = (uint32_t)cvt2_fp8<PCB_DTYPE_E4M3>(__fmul_rn(ch[it].v(4), qs), __fmul_rn(ch[it].v(5), qs)) |
+                ((uint32_t)cvt2_fp8<PCB_DTYPE_E4M3>(__fmul_rn(ch[it].v(6), qs), __fmul_rn(ch[it].v(7), qs)) << 16);
           // 128-byte-swizzled K-major row r: 16-byte chunk (c16/2) XOR (r % 8).
-          *reinterpret_cast<uint2*>(aq + r * 128 + (((c16 >> 1) ^ (r & 7)) << 4) + ((c16 & 1) << 3)) = q;
+          const uint32_t dst = aq_s + (uint32_t)r * 128u + ((uint32_t)((c16 >> 1) ^ (r & 7)) << 4) + ((c16 & 1) << 3);
+          asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(dst), "r"(q.x), "r"(q.y) : "memory");
           const float deq = __frcp_rn(qs);
           if (c16 == 0) slot[r] = deq;
           const int row = mb * BM + r;
