@@ -168,7 +168,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           for (int kk = 0; kk < BK / UMMA_K; ++kk) {
             const uint64_t a_off = (uint64_t)(kk * UMMA_K >> 4);
             const uint64_t b_off = B_MN ? (uint64_t)(kk * UMMA_K * 128 >> 4) : (uint64_t)(kk * UMMA_K >> 4);
-            umma_f8(d_tmem, adesc0 + a_off, bdesc0 + b_off, IDESC, kk > 0 ? 1u : 0u);
+            if (!(p.debug_flags & 2)) umma_f8(d_tmem, adesc0 + a_off, bdesc0 + b_off, IDESC, kk > 0 ? 1u : 0u);
           }
           umma_commit(bar_empty + 8 * stage);
           umma_commit(bar_tfull + 8 * abuf);
@@ -205,6 +205,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         uint8_t* aq = smem + S::OFF_A + stage * S::A_BYTES;
         float* slot = ring + (gq % kScaleRing) * BM;
         const int kcol = ks * BK + c16 * 8;
+        if (!(p.debug_flags & 8)) {
         // All 16 row-pair loads first (explicit shared-memory loads), then the
         // reductions and casts, so the loads overlap instead of serialising.
         const uint32_t xs_s = smem_u32(xs) + (uint32_t)(qw * 32 + half) * 256u + (uint32_t)c16 * 16u;
@@ -245,6 +246,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
                                         (long long)row * p.sxqm + kcol) = q;
             if (p.xs && c16 == 0) p.xs[(long long)b * p.sxsb + (long long)row * p.sxsm + (long long)ks * p.sxsk] = deq;
           }
+        }
         }
         fence_proxy_async_smem();  // generic-proxy smem writes -> visible to the tensor core
         __syncwarp();
@@ -307,6 +309,12 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         }
         const float s_row = ring[slot * BM + row_in_tile];
         tc_fence_after();
+        if (p.debug_flags & 1) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar_tempty + 8 * abuf);
+          ++acc_cnt;
+          continue;
+        }
         const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN + half * EPI_COLS;
 #pragma unroll
         for (int c = 0; c < EPI_COLS / 32; ++c) {

@@ -607,6 +607,8 @@ int pcb_quant_bmm_fused(const void* x, int x_dtype, int64_t sxb, int64_t sxm, in
   p.sxsm = sxsm;
   p.sxsk = sxsk;
   p.eps = eps;
+  // Profiling knob: PCB200_BMM_DEBUG (1 epilogue math, 2 MMAs, 8 quantizer work skipped).
+  if (const char* dbg = std::getenv("PCB200_BMM_DEBUG")) p.debug_flags = std::atoi(dbg);
   cudaStream_t s = (cudaStream_t)stream;
   const int sm = di.sm_count;
   if (x_dtype == PCB_DTYPE_BF16) {
