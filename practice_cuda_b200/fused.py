@@ -31,8 +31,16 @@ def quant_bmm_fused(
     activation: str = "none",
     eps: float = 1e-12,
     return_quantized: bool = False,
+    fuse: Optional[bool] = None,
 ):
-    """``act(quant_1x128(x) @ b + bias)``.  ``x`` is [B, M, K] (or [M, K]),
+    """``act(quant_1x128(x) @ b + bias)``.
+
+    The fused kernel quantizes each 128x128 activation tile inside every
+    output tile that consumes it, so its quantization work grows with the
+    number of 128-wide output column blocks.  ``fuse=None`` (default) uses it
+    when N <= 256 (at most two column blocks) and otherwise runs the 1x128
+    quantizer once followed by the per-block GEMM (two launches, identical
+    results); ``fuse=True`` / ``False`` forces either path.  ``x`` is [B, M, K] (or [M, K]),
     K contiguous; ``b`` is an e4m3 QuantResult [B, K, N] with 128-deep K blocks.
     With ``return_quantized`` also returns the QuantResult of ``x``."""
     if activation not in ("none", "gelu"):
@@ -68,6 +76,23 @@ def quant_bmm_fused(
         raise ValueError("B must be per-block (128 x block_n) or per-channel (channel_axis=-1)")
     if out is None:
         out = torch.empty((batch, m, n), device=x.device, dtype=out_dtype)
+    if fuse is None:
+        fuse = n <= 256
+    if not fuse:
+        from .impls.b200_per_block import b200_per_block_bmm, b200_per_block_quant
+
+        qx = b200_per_block_quant(x, block_m=1, block_n=128, eps=eps)
+        if b.granularity == "block":
+            b200_per_block_bmm(qx, b, out_dtype=out_dtype, bias=bias, out=out, activation=activation)
+        else:
+            # per-channel B with 1x128 A: per-block BMM with a 128 x 1 view of the B scales
+            bscale = sb.unsqueeze(1).expand(batch, (k + 127) // 128, n).contiguous()
+            qb2 = QuantResult(b.tensor, bscale, b.impl, "block", {"block_m": 128, "block_n": 1})
+            b200_per_block_bmm(qx, qb2, out_dtype=out_dtype, bias=bias, out=out, activation=activation)
+        if squeeze:
+            out = out[0]
+            qx = QuantResult(qx.tensor[0], qx.dequant_scale[0], qx.impl, qx.granularity, dict(qx.meta))
+        return (out, qx) if return_quantized else out
     if bias is not None and bias.shape != (batch, m, n):
         raise ValueError(f"bias must have shape {(batch, m, n)}, got {tuple(bias.shape)}")
     xq = xs = None
