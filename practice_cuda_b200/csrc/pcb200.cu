@@ -99,6 +99,24 @@ int launch_groups(const void* x, int xt, int64_t batch, int64_t m, int64_t n, in
   const bool vec_ok = sxn == 1 && syn == 1 && n % vec == 0 && gn % vec == 0 && aligned(x, 16) &&
                       (sxm * es) % 16 == 0 && (batch == 1 || (sxb * es) % 16 == 0) && aligned(y, vec) &&
                       sym % vec == 0 && (batch == 1 || syb % vec == 0);
+  if (gn == 1 && gm > 1 && sxn == 1 && syn == 1 && n % vec == 0 && aligned(x, 16) && (sxm * es) % 16 == 0 &&
+      (batch == 1 || (sxb * es) % 16 == 0) && aligned(y, vec) && sym % vec == 0 && (batch == 1 || syb % vec == 0) &&
+      gm <= (int64_t)1 << 30) {
+    // Column blocks (gm x 1, e.g. 128 x 1) of a row-major tensor: one CTA per
+    // (64-or-32-column strip, row slab), coalesced along the row.
+    const int sw = 8 * vec;
+    quant::ColArgs a{x, sxb, sxm, y, syb, sym, scale, ssb, ssn, m, n, (int)gm, eps, ssm};
+    return dispatch_xy(xt, yt, [&](auto xc, auto yc) -> int {
+      constexpr int XT = decltype(xc)::value;
+      constexpr int YT = decltype(yc)::value;
+      const dim3 grid((unsigned)((n + sw - 1) / sw), (unsigned)groups_m, (unsigned)batch);
+      if (mode == quant::kDeqReciprocal)
+        quant::quant_cols_cluster_kernel<XT, YT, true><<<grid, quant::kThreads, 0, stream>>>(a);
+      else
+        return fail(PCB_ERR_UNSUPPORTED, "column-slab quantization is per-block only");
+      return check_launch("quant_cols_cluster_kernel (slab)");
+    });
+  }
   const int64_t cpg = gn / vec;
   if (vec_ok && gm == 1 && cpg <= 32 && (32 % cpg) == 0) {
     // Row groups of at most one warp (1x128 and narrower): contiguous row spans.
@@ -428,7 +446,7 @@ int pcb_quant_per_channel(const void* x, int x_dtype, int64_t batch, int64_t m, 
   }
   const int sw = 8 * vec;
   const int cl = (int)std::min<int64_t>(8, std::max<int64_t>(1, (m + 255) / 256));
-  quant::ColArgs a{x, sxb, sxm, y, syb, sym, scale, ssb, ssc, m, n, (int)((m + cl - 1) / cl), eps};
+  quant::ColArgs a{x, sxb, sxm, y, syb, sym, scale, ssb, ssc, m, n, (int)((m + cl - 1) / cl), eps, 0};
   return dispatch_xy(x_dtype, y_dtype, [&](auto xc, auto yc) -> int {
     constexpr int XT = decltype(xc)::value;
     constexpr int YT = decltype(yc)::value;

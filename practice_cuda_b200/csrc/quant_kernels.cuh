@@ -345,9 +345,14 @@ struct ColArgs {
   int64_t m, n;
   int rows_per_cta;
   float eps;
+  int64_t ss_slab;  // SLAB mode: scale stride between row slabs
 };
 
-template <int XT, int YT>
+// SLAB = false: per-channel columns (one scale per column over all rows, the
+//               rows split over a cluster, dequant = amax / fp8_max).
+// SLAB = true:  per-block (rows_per_cta x 1) blocks, e.g. 128 x 1: CTA
+//               blockIdx.y owns one row slab, dequant = 1 / quant_scale.
+template <int XT, int YT, bool SLAB = false>
 __global__ void __launch_bounds__(kThreads) quant_cols_cluster_kernel(const ColArgs args) {
   using C = Chunk<XT>;
   using T = typename C::T;
@@ -359,10 +364,12 @@ __global__ void __launch_bounds__(kThreads) quant_cols_cluster_kernel(const ColA
   __shared__ uint32_t partial[SW];
   __shared__ float qs_s[SW];
 
-  cg::cluster_group cluster = cg::this_cluster();
-  const int rank = (int)cluster.block_rank();
-  const int nranks = (int)cluster.num_blocks();
   const float fp8_max = Fp8Max<YT>::value;
+  int rank = 0, nranks = 1;
+  if constexpr (!SLAB) {
+    rank = (int)cg::this_cluster().block_rank();
+    nranks = (int)cg::this_cluster().num_blocks();
+  }
 
   const int64_t b = blockIdx.z;
   const int64_t col0 = (int64_t)blockIdx.x * SW;
@@ -370,7 +377,8 @@ __global__ void __launch_bounds__(kThreads) quant_cols_cluster_kernel(const ColA
   const int rl = threadIdx.x / CHUNK_COLS;
   const int64_t col = col0 + (int64_t)cc * VEC;
   const bool col_ok = col < args.n;  // n % VEC == 0, so a chunk is all-in or all-out
-  const int64_t r_begin = (int64_t)rank * args.rows_per_cta;
+  const int64_t slab = SLAB ? (int64_t)blockIdx.y : (int64_t)rank;
+  const int64_t r_begin = slab * args.rows_per_cta;
   const int64_t r_end = min(args.m, r_begin + args.rows_per_cta);
   const T* xb = static_cast<const T*>(args.x) + b * args.sxb;
   uint8_t* yb = static_cast<uint8_t*>(args.y) + b * args.syb;
@@ -394,17 +402,33 @@ __global__ void __launch_bounds__(kThreads) quant_cols_cluster_kernel(const ColA
     for (int l = 0; l < ROW_LANES; ++l) v = max(v, red[l][threadIdx.x]);
     partial[threadIdx.x] = v;
   }
-  cluster.sync();
+  if constexpr (SLAB) {
+    __syncthreads();
+  } else {
+    cg::this_cluster().sync();
+  }
   if (threadIdx.x < SW) {
     uint32_t v = 0;
-    for (int r = 0; r < nranks; ++r) v = max(v, cluster.map_shared_rank(partial, r)[threadIdx.x]);
+    if constexpr (SLAB) {
+      v = partial[threadIdx.x];
+    } else {
+      for (int r = 0; r < nranks; ++r) v = max(v, cg::this_cluster().map_shared_rank(partial, r)[threadIdx.x]);
+    }
     const float safe = clamp_min_eps(__uint_as_float(v), args.eps);
     const float qs = quant_scale_from_amax(safe, fp8_max);
     qs_s[threadIdx.x] = qs;
     const int64_t c = col0 + threadIdx.x;
-    if (rank == 0 && c < args.n) args.scale[b * args.ssb + c * args.ssc] = __fdiv_rn(safe, fp8_max);
+    if (SLAB && c < args.n) {
+      args.scale[b * args.ssb + slab * args.ss_slab + c * args.ssc] = __frcp_rn(qs);
+    } else if (!SLAB && rank == 0 && c < args.n) {
+      args.scale[b * args.ssb + c * args.ssc] = __fdiv_rn(safe, fp8_max);
+    }
   }
-  cluster.sync();  // remote reads of `partial` are done; qs_s visible to the CTA
+  if constexpr (SLAB) {
+    __syncthreads();
+  } else {
+    cg::this_cluster().sync();  // remote reads of `partial` are done; qs_s visible to the CTA
+  }
   if (col_ok) {
     for (int64_t r = r_begin + rl; r < r_end; r += ROW_LANES) {
       C ch;
