@@ -1,0 +1,124 @@
+"""FSDP2 all-gather of per-block FP8 weights (BASELINE cfg5; SURVEY next-step 2).
+
+A linear weight wrapped in :class:`FP8AllGatherWeight` keeps its
+high-precision master values in the FSDP shard, but when FSDP2 unshards it the
+shard is first quantized in 128x128 tiles (pcb_quant_per_block) and the
+all-gather carries the fp8 bytes plus the fp32 tile scales -- about half the
+bytes of a bf16 all-gather.  After the all-gather the unsharded parameter is a
+:class:`~practice_cuda_b200.fp8_linear.BlockFP8Weight` that
+:class:`~practice_cuda_b200.fp8_linear.FP8BlockLinear` feeds straight into the
+FP8 GEMMs.
+
+This is the per-block counterpart of the reference's
+``WeightWithDynamicFloat8CastTensor`` FSDP hooks
+(``fp8_training/fp8_bench/modules/float8/fsdp_utils.py:271-386``), which
+support tensorwise / axiswise scales only (its per-block all-gather is an
+``assert False``, ``modules/per_block.py:102-104``).  Per-block scales are local
+to a tile, so unlike tensorwise scaling no amax all-reduce is needed; the
+only constraint is that every rank's row shard is a whole number of 128-row
+tiles (``out_features`` divisible by ``128 * world_size``).
+"""
+
+from __future__ import annotations
+
+from typing import Any, Optional
+
+import torch
+import torch.nn as nn
+from torch.utils._pytree import tree_map_only
+
+from .fp8_linear import E4M3, BlockFP8Weight, FP8BlockLinear, quantize_weight
+
+# Ops whose tensor outputs stay wrapped (views, copies, new tensors of the
+# same role); everything else (optimizer math, reductions) returns plain tensors.
+_PRESERVE = {
+    torch.ops.aten.empty_like.default,
+    torch.ops.aten.new_zeros.default,
+    torch.ops.aten.new_empty.default,
+    torch.ops.aten.slice.Tensor,
+    torch.ops.aten.copy_.default,
+    torch.ops.aten.view.default,
+    torch.ops.aten.as_strided.default,
+    torch.ops.aten._to_copy.default,
+    torch.ops.aten._pin_memory.default,
+    torch.ops.aten.split.Tensor,
+    torch.ops.aten.clone.default,
+    torch.ops.aten.detach.default,
+    torch.ops.aten.alias.default,
+}
+
+
+class FP8AllGatherWeight(torch.Tensor):
+    """High-precision weight whose FSDP2 all-gather is per-block FP8."""
+
+    @staticmethod
+    def __new__(cls, tensor: torch.Tensor):
+        return torch.Tensor._make_wrapper_subclass(
+            cls,
+            tensor.size(),
+            strides=tensor.stride(),
+            storage_offset=tensor.storage_offset(),
+            dtype=tensor.dtype,
+            layout=tensor.layout,
+            device=tensor.device,
+            requires_grad=tensor.requires_grad,
+        )
+
+    def __init__(self, tensor: torch.Tensor):
+        self._tensor = tensor
+
+    def __repr__(self):
+        return f"FP8AllGatherWeight({self._tensor!r})"
+
+    def __tensor_flatten__(self):
+        return ["_tensor"], None
+
+    @staticmethod
+    def __tensor_unflatten__(inner, meta, outer_size, outer_stride):
+        return FP8AllGatherWeight(inner["_tensor"])
+
+    @classmethod
+    def __torch_dispatch__(cls, func, types, args=(), kwargs=None):
+        kwargs = kwargs or {}
+        args, kwargs = tree_map_only(FP8AllGatherWeight, lambda t: t._tensor, (args, kwargs))
+        out = func(*args, **kwargs)
+        if func not in _PRESERVE:
+            return out
+        return tree_map_only(torch.Tensor, FP8AllGatherWeight, out)
+
+    # ---- FSDP2 all-gather extension -------------------------------------------
+    def fsdp_pre_all_gather(self, mesh, outer_size, outer_stride, module, mp_policy):
+        shard = self._tensor
+        if shard.shape[0] % 128 != 0:
+            raise ValueError(
+                f"per-block FP8 all-gather needs whole 128-row tiles per rank; shard has {shard.shape[0]} rows "
+                f"(out_features {outer_size[0]} over {mesh.size()} ranks)"
+            )
+        data, scale = quantize_weight(shard)
+        return (data.view(torch.uint8), scale), None
+
+    def fsdp_post_all_gather(
+        self,
+        all_gather_outputs: tuple[torch.Tensor, ...],
+        metadata: Any,
+        param_dtype: torch.dtype,
+        *,
+        out: Optional[torch.Tensor] = None,
+    ):
+        data_u8, scale = all_gather_outputs
+        data = data_u8.view(E4M3)
+        if out is not None:
+            # Storage of the inner tensors was re-filled in place by FSDP.
+            out._data = data
+            out._scale = scale
+            return None
+        return BlockFP8Weight(data, scale, param_dtype), (data_u8, scale)
+
+
+def enable_fp8_all_gather(module: nn.Module) -> nn.Module:
+    """Wrap the weight of every :class:`FP8BlockLinear` in ``module`` so that
+    FSDP2 all-gathers it as per-block FP8 (call before ``fully_shard``)."""
+    for m in module.modules():
+        if isinstance(m, FP8BlockLinear) and not isinstance(m.weight, FP8AllGatherWeight):
+            m.weight = nn.Parameter(FP8AllGatherWeight(m.weight.data), requires_grad=m.weight.requires_grad)
+    return module
