@@ -95,6 +95,16 @@ class FP8AllGatherWeight(torch.Tensor):
                 f"(out_features {outer_size[0]} over {mesh.size()} ranks)"
             )
         data, scale = quantize_weight(shard)
+        if mesh.size() == 1:
+            # FSDP2's single-rank path takes exactly one all-gather input, so
+            # the scales ride in extra uint8 rows appended to the fp8 rows.
+            rows, cols = data.shape
+            sbytes = scale.numel() * 4
+            extra = (sbytes + cols - 1) // cols
+            packed = torch.zeros((rows + extra, cols), dtype=torch.uint8, device=data.device)
+            packed[:rows].copy_(data.view(torch.uint8))
+            packed[rows:].view(-1)[:sbytes].copy_(scale.reshape(-1).view(torch.uint8))
+            return (packed,), {"rows": rows, "scale_shape": tuple(scale.shape)}
         return (data.view(torch.uint8), scale), None
 
     def fsdp_post_all_gather(
@@ -105,14 +115,24 @@ class FP8AllGatherWeight(torch.Tensor):
         *,
         out: Optional[torch.Tensor] = None,
     ):
-        data_u8, scale = all_gather_outputs
+        if metadata is not None:  # single rank: fp8 rows followed by the packed scales
+            (packed,) = all_gather_outputs
+            rows = metadata["rows"]
+            shape = metadata["scale_shape"]
+            data_u8 = packed[:rows]
+            nbytes = shape[0] * shape[1] * 4
+            scale = packed[rows:].reshape(-1)[:nbytes].view(torch.float32).view(shape)
+            inner = (packed,)
+        else:
+            data_u8, scale = all_gather_outputs
+            inner = (data_u8, scale)
         data = data_u8.view(E4M3)
         if out is not None:
             # Storage of the inner tensors was re-filled in place by FSDP.
             out._data = data
             out._scale = scale
             return None
-        return BlockFP8Weight(data, scale, param_dtype), (data_u8, scale)
+        return BlockFP8Weight(data, scale, param_dtype), inner
 
 
 def enable_fp8_all_gather(module: nn.Module) -> nn.Module:
