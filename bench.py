@@ -52,6 +52,11 @@ def parse_args():
     ap.add_argument("--batches", type=int, default=GLOBAL_B, help="global batch count (cfg3: 32)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["cfg3", "cfg5"], default="cfg3",
+                    help="cfg3: per-block BMM step (default); cfg5: FSDP2 FP8 training step of the Llama decoder")
+    ap.add_argument("--cfg5-linear", choices=["fp8", "bf16"], default="fp8",
+                    help="cfg5 only: per-block FP8 linears (default) or the bf16 baseline")
+    ap.add_argument("--layers", type=int, default=8, help="cfg5 only: decoder layers (BASELINE: 8)")
     ap.add_argument("--fp8-peak", action="store_true",
                     help="only measure the FP8 dense peak with torch._scaled_mm (cuBLASLt) at 8192^3")
     return ap.parse_args()
@@ -269,6 +274,96 @@ def measure_fp8_peak() -> None:
                       "shape": [n, n, n], "clocks": clocks.stop(), "how": "torch._scaled_mm (cuBLASLt) e4m3, bf16 out"}))
 
 
+def run_cfg5(args, world: int, rank: int, local_rank: int) -> None:
+    """BASELINE cfg5: one FSDP2 training step (forward, backward, AdamW) of the
+    random-init Llama-style decoder on seq 4096 x batch 1 per GPU, synthetic
+    token ids.  Linear layers are per-block FP8 (forward, dgrad, wgrad) with
+    the FP8 weight + scale all-gather; ``--cfg5-linear bf16`` runs the same
+    model with bf16 linears and bf16 all-gather as the comparison point.
+    Reports model TFLOP/s per GPU as 6 * tokens * linear params / step time
+    (the reference's estimate, bench_fsdp2.py:179-187) plus the causal
+    attention FLOPs separately."""
+    import torch.distributed as dist
+    from torch.distributed.fsdp import MixedPrecisionPolicy, fully_shard
+
+    from practice_cuda_b200.fp8_linear import FP8BlockLinear
+    from practice_cuda_b200.fsdp_fp8 import enable_fp8_all_gather
+    from practice_cuda_b200.llama import Llama, LlamaConfig
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    dist.init_process_group("nccl", device_id=device, rank=rank, world_size=world)
+    cfg = LlamaConfig(n_layers=args.layers)
+    with torch.device(device):
+        model = Llama(cfg)
+    model.init_weights(seed=0)
+    if args.cfg5_linear == "bf16":
+        for mod in list(model.modules()):
+            for name, child in list(mod.named_children()):
+                if isinstance(child, FP8BlockLinear):
+                    lin = torch.nn.Linear(child.in_features, child.out_features, bias=False, device=device)
+                    lin.weight = child.weight
+                    setattr(mod, name, lin)
+    else:
+        enable_fp8_all_gather(model)
+    mp = MixedPrecisionPolicy(param_dtype=torch.bfloat16, reduce_dtype=torch.float32)
+    for layer in model.layers:
+        fully_shard(layer, mp_policy=mp)
+    fully_shard(model, mp_policy=mp)
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-4, fused=True)
+    g = torch.Generator(device=device).manual_seed(1234 + rank)
+    tokens = torch.randint(0, cfg.vocab, (1, cfg.seq_len + 1), device=device, generator=g)
+
+    def step():
+        logits = model(tokens[:, :-1])
+        loss = torch.nn.functional.cross_entropy(logits.float().view(-1, cfg.vocab), tokens[:, 1:].reshape(-1))
+        loss.backward()
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+        return loss
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.steps):
+        loss = step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = torch.tensor([s.elapsed_time(e) / args.steps], device=device, dtype=torch.float64)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = ms.item()
+    tokens_per_gpu = cfg.seq_len
+    linear_flop = 6 * tokens_per_gpu * cfg.linear_params()
+    attn_flop = 3 * cfg.n_layers * 2 * 2 * cfg.seq_len * cfg.seq_len * cfg.dim / 2  # causal, fwd + 2x bwd
+    if rank == 0:
+        print(json.dumps({
+            "metric": "fsdp2_train_model_tflops_per_gpu",
+            "value": linear_flop / (ms * 1e-3) / 1e12,
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "dtype": "per-block e4m3 linears" if args.cfg5_linear == "fp8" else "bf16 linears",
+            "data": "synthetic token ids, random-init weights",
+            "config": {"workload": "cfg5 FSDP2 training step", "layers": cfg.n_layers, "dim": cfg.dim,
+                       "heads": cfg.n_heads, "ffn": cfg.ffn_dim, "vocab": cfg.vocab, "seq_len": cfg.seq_len,
+                       "batch_per_gpu": 1, "parallelism": f"fsdp2 x{world}",
+                       "all_gather": "per-block fp8 + fp32 scales" if args.cfg5_linear == "fp8" else "bf16",
+                       "lm_head_and_embedding": "bf16"},
+            "linear_tflop_per_gpu_step": linear_flop / 1e12,
+            "attention_tflop_per_gpu_step": attn_flop / 1e12,
+            "tokens_per_s": world * tokens_per_gpu / (ms * 1e-3),
+            "final_loss": float(loss.item()),
+        }), flush=True)
+    dist.destroy_process_group()
+
+
 # ------------------------------------------------------------------- main ---
 def main() -> None:
     args = parse_args()
@@ -280,6 +375,9 @@ def main() -> None:
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.workload == "cfg5":
+        run_cfg5(args, world, rank, local_rank)
         return
 
     import torch.distributed as dist
