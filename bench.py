@@ -290,6 +290,8 @@ def run_cfg5(args, world: int, rank: int, local_rank: int) -> None:
     from practice_cuda_b200.fsdp_fp8 import enable_fp8_all_gather
     from practice_cuda_b200.llama import Llama, LlamaConfig
 
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29555")
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     dist.init_process_group("nccl", device_id=device, rank=rank, world_size=world)
