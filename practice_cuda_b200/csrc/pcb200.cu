@@ -689,11 +689,7 @@ int pcb_bmm_scaled(const void* a, int64_t sab, int64_t sam, int64_t sak, const v
   CUtensorMap ta, tb;
   // 128x256 tiles (128x128 when N <= 128): 32 KB of fp8 operands per
   // 128-deep K stage feed 8.4 MFLOP, which keeps L2 traffic per FLOP low.
-  // Per-column scales (e.g. the 128x1 operands of a weight gradient) cost an
-  // extra smem read and multiply per element; those tiles stay 128x128 so the
-  // epilogue keeps its accumulators in registers.
-  const bool col_uniform_req = (!scale_b || ssbn == 0 || qbn % 128 == 0 || qbn >= n);
-  const int bn = (n > 128 && col_uniform_req) ? 256 : 128;
+  const int bn = (n > 128) ? 256 : 128;
   // 256x256 tiles on a CTA pair (cta_group::2) when M spans two 128-row
   // halves and the tile has a single K group (per-channel / per-tensor): each
   // CTA stages its own 128 A rows and half of the B tile.  With per-block
