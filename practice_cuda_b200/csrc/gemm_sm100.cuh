@@ -516,6 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half = ew >> 2;               // column half
     const int row_in_tile = quarter * 32 + lane;
     float* colscale = reinterpret_cast<float*>(smem + S::OFF_COLSCALE) + ew * EPI_COLS;
+    const uint32_t colscale_s = smem_u32(colscale);
     uint32_t acc_cnt = 0;
     bool ok = true;
     // The tmem-empty barrier lives in the leader; the follower arrives remotely.
@@ -622,15 +623,28 @@ __global__ void __launch_bounds__(kThreads, 1)
               tmem_ld16_nowait(taddr + c * 16, v);
               tmem_wait_ld();
 #pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                float2 s2;
-                if constexpr (COL_UNIFORM) {
-                  s2 = make_float2(s_row * s_col, s_row * s_col);
-                } else {
-                  s2 = make_float2(s_row * colscale[c * 16 + 2 * i], s_row * colscale[c * 16 + 2 * i + 1]);
+              if constexpr (COL_UNIFORM) {
+                const float2 s2 = make_float2(s_row * s_col, s_row * s_col);
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                  acc[c * 8 + i] = __ffma2_rn(make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])), s2,
+                                              acc[c * 8 + i]);
+              } else {
+                // 16 column scales of this chunk: four broadcast 16-byte shared loads.
+                const float2 r2 = make_float2(s_row, s_row);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  float4 cs4;
+                  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                               : "=f"(cs4.x), "=f"(cs4.y), "=f"(cs4.z), "=f"(cs4.w)
+                               : "r"(colscale_s + (uint32_t)(c * 16 + 4 * q) * 4u));
+                  const float2 sa = __fmul2_rn(make_float2(cs4.x, cs4.y), r2);
+                  const float2 sb2 = __fmul2_rn(make_float2(cs4.z, cs4.w), r2);
+                  acc[c * 8 + 2 * q] = __ffma2_rn(
+                      make_float2(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1])), sa, acc[c * 8 + 2 * q]);
+                  acc[c * 8 + 2 * q + 1] = __ffma2_rn(
+                      make_float2(__uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3])), sb2, acc[c * 8 + 2 * q + 1]);
                 }
-                acc[c * 8 + i] = __ffma2_rn(make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])), s2,
-                                            acc[c * 8 + i]);
               }
             }
             tc_fence_before();
