@@ -358,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int first_tile = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
   // Waits whose arrival may come from the peer CTA poll without suspending
   // (flag 16 switches back to the suspending try_wait, profiling only).
-  const bool spin = PAIR && !(p.debug_flags & 16);
+  const bool spin = (PAIR && !(p.debug_flags & 16)) || (p.debug_flags & 32);
   auto wait = [&](uint32_t bar, uint32_t parity, int site) -> bool {
     return spin ? mbar_spin_bounded(bar, parity, abort_flag, site) : mbar_wait_bounded(bar, parity, abort_flag, site);
   };
