@@ -9,8 +9,12 @@
 //   warps 4-11  epilogue: two warpgroups; warpgroup h owns tile columns
 //               [h*BN/2, (h+1)*BN/2), warp (w % 4) owns TMEM lanes / rows
 //               [32*(w%4), 32*(w%4)+32).
-// TMEM holds two accumulator buffers of BN fp32 columns each, so the MMA of
-// K-group g+1 runs while the epilogue promotes group g.
+// Tiles are 128 x BN (BN = 128 or 256).  TMEM holds 512 / BN accumulator
+// buffers of BN fp32 columns, so the MMA of K-group g+1 runs while the
+// epilogue promotes group g.  With PAIR the tile is 256 x BN on a CTA pair
+// (cta_group::2): each CTA stages its own 128 A rows and half of the B
+// columns, the even CTA issues the MMAs for both and multicasts its commits,
+// and both CTAs' epilogues read their own TMEM half.
 #pragma once
 
 #include "common.cuh"
@@ -66,7 +70,8 @@ struct Params {
   float* xs;
   long long sxsb, sxsm, sxsk;
   float eps;
-  int debug_flags;  // profiling only: 1 = epilogue skips its math, 2 = no MMAs issued, 4 = MMA ignores tmem-empty
+  int debug_flags;  // profiling only: 1 = epilogue skips its math, 2 = no MMAs issued, 4 = MMA ignores tmem-empty,
+                   // 8 = fused quantizer skipped, 16 = no spin waits on a pair, 32 = spin waits on one CTA
 };
 
 // ---------------------------------------------------------------------------
