@@ -27,6 +27,7 @@ enum ErrorSite : int {
   SITE_FUSED_PRODUCER = 5,
   SITE_FUSED_MMA = 6,
   SITE_FUSED_EPILOGUE = 7,
+  SITE_QUANT_TILE = 8,
 };
 
 __device__ __forceinline__ void report_error(int code, int site) {

@@ -13,6 +13,7 @@
 #include "gemm_sm100.cuh"
 #include "quant_kernels.cuh"
 #include "gemm_fused_sm100.cuh"
+#include "quant_tile_tma.cuh"
 
 using namespace pcb;
 
@@ -87,6 +88,9 @@ int dispatch_xy(int xt, int yt, F&& f) {
 // ---------------------------------------------------------------------------
 // Grouped quantization (per-block and per-channel rows share this driver).
 // ---------------------------------------------------------------------------
+bool make_map_x16(CUtensorMap* map, const void* base, int dt, uint64_t inner, uint64_t outer, uint64_t batch,
+                  uint64_t outer_stride_bytes, uint64_t batch_stride_bytes);
+
 int launch_groups(const void* x, int xt, int64_t batch, int64_t m, int64_t n, int64_t sxb, int64_t sxm, int64_t sxn,
                   void* y, int yt, int64_t syb, int64_t sym, int64_t syn, float* scale, int64_t ssb, int64_t ssm,
                   int64_t ssn, int64_t gm, int64_t gn, int mode, float eps, cudaStream_t stream) {
@@ -151,6 +155,30 @@ int launch_groups(const void* x, int xt, int64_t batch, int64_t m, int64_t n, in
                               : go(quant::quant_rowspan_kernel<XT, YT, 32, CH, quant::kDeqDivide>);
       }
     });
+  }
+  if (vec_ok && gm == 128 && gn == 128 && (xt == PCB_DTYPE_BF16 || xt == PCB_DTYPE_F16) && m <= INT32_MAX &&
+      n <= INT32_MAX && batch <= INT32_MAX) {
+    // 128x128 tiles of a 16-bit tensor: TMA-staged persistent kernel.
+    CUtensorMap tm;
+    if (make_map_x16(&tm, x, xt, (uint64_t)n, (uint64_t)m, (uint64_t)batch, (uint64_t)sxm * 2, (uint64_t)sxb * 2)) {
+      quant::TileArgs a{y, syb, sym, scale, ssb, ssm, ssn, m, n, groups_m, groups_n, num_groups, eps};
+      const unsigned grid = (unsigned)std::min<int64_t>(num_groups, di.sm_count);
+      auto go = [&](auto kernel) -> int {
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, quant::kTileSmem);
+        kernel<<<grid, quant::kThreads, quant::kTileSmem, stream>>>(tm, a);
+        return check_launch("quant_tile128_tma_kernel");
+      };
+      return dispatch_xy(xt, yt, [&](auto xc, auto yc) -> int {
+        constexpr int XT = decltype(xc)::value;
+        constexpr int YT = decltype(yc)::value;
+        if constexpr (XT == PCB_DTYPE_BF16 || XT == PCB_DTYPE_F16) {
+          return mode == quant::kDeqReciprocal ? go(quant::quant_tile128_tma_kernel<XT, YT, quant::kDeqReciprocal>)
+                                               : go(quant::quant_tile128_tma_kernel<XT, YT, quant::kDeqDivide>);
+        } else {
+          return fail(PCB_ERR_UNSUPPORTED, "unreachable");
+        }
+      });
+    }
   }
   if (vec_ok) {
     quant::GroupArgs a{x, sxb, sxm, y, syb, sym, scale, ssb, ssm, ssn, batch, m, n, gm, gn, groups_m, groups_n,

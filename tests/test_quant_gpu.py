@@ -53,6 +53,24 @@ def test_per_block_vs_oracle(dtype, shape, bm, bn):
     assert_scales_equal(q.dequant_scale, s_ref, f"{shape} {bm}x{bn} {dtype}")
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_per_block_128x128_strided_rows_and_many_tiles(dtype):
+    """128x128 tiles of a column-sliced view (row stride > n) and a tensor with
+    many more tiles than SMs, so every CTA's staging ring wraps several times."""
+    base = synthetic((3, 300, 392), outliers=True, seed=31, dtype=dtype)
+    x = base.to(DEV)[:, :, :264]
+    assert x.stride(1) == 392
+    q = _per_block(x, 128, 128)
+    y_ref, s_ref = oracle.per_block_quant(base[:, :, :264].contiguous(), block_m=128, block_n=128)
+    assert_bytes_equal(q.tensor, y_ref, f"strided {dtype}")
+    assert_scales_equal(q.dequant_scale, s_ref, f"strided {dtype}")
+    big = synthetic((6, 1024, 2048), seed=32, dtype=dtype)
+    q = _per_block(big, 128, 128)
+    y_ref, s_ref = oracle.per_block_quant(big, block_m=128, block_n=128)
+    assert_bytes_equal(q.tensor, y_ref, f"many tiles {dtype}")
+    assert_scales_equal(q.dequant_scale, s_ref, f"many tiles {dtype}")
+
+
 def test_per_block_cfg1_full_size():
     """BASELINE cfg1 at full size: x [4096,7168] 1x128 and w [7168,7168] 128x128."""
     x = synthetic((4096, 7168), outliers=True, seed=0)
