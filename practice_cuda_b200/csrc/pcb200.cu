@@ -121,6 +121,37 @@ int launch_groups(const void* x, int xt, int64_t batch, int64_t m, int64_t n, in
       return check_launch("quant_cols_cluster_kernel (slab)");
     });
   }
+  if (vec_ok && (gm == 128 || gm == 1) && gn == 128 && (xt == PCB_DTYPE_BF16 || xt == PCB_DTYPE_F16) &&
+      m <= INT32_MAX && n <= INT32_MAX && batch <= INT32_MAX) {
+    // 128x128 or 1x128 blocks of a 16-bit tensor: TMA-staged persistent kernel
+    // over 128x128 tiles.
+    CUtensorMap tm;
+    if (make_map_x16(&tm, x, xt, (uint64_t)n, (uint64_t)m, (uint64_t)batch, (uint64_t)sxm * 2, (uint64_t)sxb * 2)) {
+      const int64_t num_tiles = batch * ((m + 127) / 128) * groups_n;
+      quant::TileArgs a{y, syb, sym, scale, ssb, ssm, ssn, m, n, groups_m, groups_n, num_tiles, eps};
+      auto go = [&](auto kernel, auto cfg) -> int {
+        using Cfg = decltype(cfg);
+        const unsigned grid = (unsigned)std::min<int64_t>(num_tiles, (int64_t)di.sm_count * Cfg::CTAS_PER_SM);
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+        kernel<<<grid, quant::kThreads, Cfg::SMEM, stream>>>(tm, a);
+        return check_launch("quant_tile128_tma_kernel");
+      };
+      return dispatch_xy(xt, yt, [&](auto xc, auto yc) -> int {
+        constexpr int XT = decltype(xc)::value;
+        constexpr int YT = decltype(yc)::value;
+        if constexpr (XT == PCB_DTYPE_BF16 || XT == PCB_DTYPE_F16) {
+          constexpr int R = quant::kDeqReciprocal, D = quant::kDeqDivide;
+          if (gm == 1)
+            return mode == R ? go(quant::quant_tile128_tma_kernel<XT, YT, R, 1>, quant::TileCfg<1>{})
+                             : go(quant::quant_tile128_tma_kernel<XT, YT, D, 1>, quant::TileCfg<1>{});
+          return mode == R ? go(quant::quant_tile128_tma_kernel<XT, YT, R, 128>, quant::TileCfg<128>{})
+                           : go(quant::quant_tile128_tma_kernel<XT, YT, D, 128>, quant::TileCfg<128>{});
+        } else {
+          return fail(PCB_ERR_UNSUPPORTED, "unreachable");
+        }
+      });
+    }
+  }
   const int64_t cpg = gn / vec;
   if (vec_ok && gm == 1 && cpg <= 32 && (32 % cpg) == 0) {
     // Row groups of at most one warp (1x128 and narrower): contiguous row spans.
@@ -155,30 +186,6 @@ int launch_groups(const void* x, int xt, int64_t batch, int64_t m, int64_t n, in
                               : go(quant::quant_rowspan_kernel<XT, YT, 32, CH, quant::kDeqDivide>);
       }
     });
-  }
-  if (vec_ok && gm == 128 && gn == 128 && (xt == PCB_DTYPE_BF16 || xt == PCB_DTYPE_F16) && m <= INT32_MAX &&
-      n <= INT32_MAX && batch <= INT32_MAX) {
-    // 128x128 tiles of a 16-bit tensor: TMA-staged persistent kernel.
-    CUtensorMap tm;
-    if (make_map_x16(&tm, x, xt, (uint64_t)n, (uint64_t)m, (uint64_t)batch, (uint64_t)sxm * 2, (uint64_t)sxb * 2)) {
-      quant::TileArgs a{y, syb, sym, scale, ssb, ssm, ssn, m, n, groups_m, groups_n, num_groups, eps};
-      const unsigned grid = (unsigned)std::min<int64_t>(num_groups, di.sm_count);
-      auto go = [&](auto kernel) -> int {
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, quant::kTileSmem);
-        kernel<<<grid, quant::kThreads, quant::kTileSmem, stream>>>(tm, a);
-        return check_launch("quant_tile128_tma_kernel");
-      };
-      return dispatch_xy(xt, yt, [&](auto xc, auto yc) -> int {
-        constexpr int XT = decltype(xc)::value;
-        constexpr int YT = decltype(yc)::value;
-        if constexpr (XT == PCB_DTYPE_BF16 || XT == PCB_DTYPE_F16) {
-          return mode == quant::kDeqReciprocal ? go(quant::quant_tile128_tma_kernel<XT, YT, quant::kDeqReciprocal>)
-                                               : go(quant::quant_tile128_tma_kernel<XT, YT, quant::kDeqDivide>);
-        } else {
-          return fail(PCB_ERR_UNSUPPORTED, "unreachable");
-        }
-      });
-    }
   }
   if (vec_ok) {
     quant::GroupArgs a{x, sxb, sxm, y, syb, sym, scale, ssb, ssm, ssn, batch, m, n, gm, gn, groups_m, groups_n,

@@ -1,4 +1,6 @@
-// 128x128 per-block quantization of 16-bit inputs, staged by TMA.
+// Per-block quantization of 16-bit inputs in 128x128 tiles staged by TMA:
+// GM = 128 quantizes each tile as one group (128x128 blocks), GM = 1 as 128
+// row groups of 128 elements (1x128 blocks).
 //
 // One persistent CTA per SM walks its share of the 128x128 tiles.  Thread 0
 // keeps kTileStages tiles (32 KB each) in flight with one
@@ -17,10 +19,16 @@
 namespace pcb {
 namespace quant {
 
-constexpr int kTileStages = 6;
 constexpr int kTileRows = 128;
 constexpr int kTileBytes = 128 * 128 * 2;
-constexpr int kTileSmem = kTileStages * kTileBytes + 1024 + 64;
+// 192 KB of tiles in flight per SM: one CTA of 6 stages for 128x128 groups;
+// 1x128 groups have more per-row work, so two CTAs of 3 stages share the SM.
+template <int GM>
+struct TileCfg {
+  static constexpr int STAGES = (GM == 1) ? 2 : 6;
+  static constexpr int CTAS_PER_SM = 6 / STAGES;
+  static constexpr int SMEM = STAGES * kTileBytes + 1024 + 64;
+};
 
 struct TileArgs {
   void* y;
@@ -28,15 +36,18 @@ struct TileArgs {
   float* scale;
   int64_t ssb, ssm, ssn;
   int64_t m, n;
-  int64_t groups_m, groups_n, num_groups;
+  int64_t groups_m, groups_n;  // groups_n = column tiles; groups_m = row groups (m for 1x128, row tiles for 128x128)
+  int64_t num_tiles;
   float eps;
 };
 
-template <int XT, int YT, int MODE>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int XT, int YT, int MODE, int GM>
+__global__ void __launch_bounds__(kThreads, TileCfg<GM>::CTAS_PER_SM)
     quant_tile128_tma_kernel(const __grid_constant__ CUtensorMap tmap, const TileArgs a) {
   static_assert(XT == PCB_DTYPE_BF16 || XT == PCB_DTYPE_F16, "16-bit inputs only");
+  static_assert(GM == 1 || GM == kTileRows, "whole-tile or per-row groups");
   using C = Chunk<XT>;
+  constexpr int kTileStages = TileCfg<GM>::STAGES;
   constexpr int CPT = kTileBytes / 16 / kThreads;  // chunks per thread (8)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -49,8 +60,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = t >> 5;
   const int64_t first = blockIdx.x;
   const int64_t step = gridDim.x;
-  const int64_t mine = first < a.num_groups ? (a.num_groups - 1 - first) / step + 1 : 0;
-  const int64_t per_batch = a.groups_m * a.groups_n;
+  const int64_t mine = first < a.num_tiles ? (a.num_tiles - 1 - first) / step + 1 : 0;
+  // Tiles are 128 rows high whatever the group height.
+  const int64_t tiles_m = (GM == 1) ? (a.groups_m + kTileRows - 1) / kTileRows : a.groups_m;
+  const int64_t per_batch = tiles_m * a.groups_n;
   const float fp8_max = Fp8Max<YT>::value;
 
   auto issue = [&](int s, int64_t g) {
@@ -85,13 +98,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       reg[i].raw = *reinterpret_cast<const uint4*>(tile + (i * kThreads + t) * 16);
       amax = max(amax, reg[i].amax_bits());
     }
+    if constexpr (GM == kTileRows) {
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-    if ((t & 31) == 0) red[it & 1][warp] = amax;
+      for (int off = 16; off > 0; off >>= 1) amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+      if ((t & 31) == 0) red[it & 1][warp] = amax;
+    }
     __syncthreads();  // every thread holds its chunks: the buffer can be refilled
-    uint32_t r = 0;
-#pragma unroll
-    for (int w = 0; w < kThreads / 32; ++w) r = max(r, red[it & 1][w]);
     if (t == 0 && it + kTileStages < mine) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       issue(s, first + (it + kTileStages) * step);
@@ -100,21 +112,46 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t g = first + it * step;
     const int64_t b = g / per_batch;
     const int64_t rem = g - b * per_batch;
-    const int64_t gi = rem / a.groups_n;
+    const int64_t gi = rem / a.groups_n;  // tile row
     const int64_t gj = rem - gi * a.groups_n;
-    const float safe = clamp_min_eps(__uint_as_float(r), a.eps);
-    const float qs = quant_scale_from_amax(safe, fp8_max);
-    if (t == 0) {
-      const float deq = (MODE == kDeqReciprocal) ? __frcp_rn(qs) : __fdiv_rn(safe, fp8_max);
-      a.scale[b * a.ssb + gi * a.ssm + gj * a.ssn] = deq;
-    }
     uint8_t* yt = static_cast<uint8_t*>(a.y) + b * a.syb + gi * kTileRows * a.sym + gj * 128;
+    if constexpr (GM == kTileRows) {
+      uint32_t r = 0;
 #pragma unroll
-    for (int i = 0; i < CPT; ++i) {
-      const int c = i * kThreads + t;
-      const int r_in = c >> 4;         // 16 chunks of 8 elements per 128-column row
-      const int col = (c & 15) * 8;
-      if (gi * kTileRows + r_in < a.m && gj * 128 + col < a.n) reg[i].template store<YT>(yt + r_in * a.sym + col, qs);
+      for (int w = 0; w < kThreads / 32; ++w) r = max(r, red[it & 1][w]);
+      const float safe = clamp_min_eps(__uint_as_float(r), a.eps);
+      const float qs = quant_scale_from_amax(safe, fp8_max);
+      if (t == 0) {
+        const float deq = (MODE == kDeqReciprocal) ? __frcp_rn(qs) : __fdiv_rn(safe, fp8_max);
+        a.scale[b * a.ssb + gi * a.ssm + gj * a.ssn] = deq;
+      }
+#pragma unroll
+      for (int i = 0; i < CPT; ++i) {
+        const int c = i * kThreads + t;
+        const int r_in = c >> 4;  // 16 chunks of 8 elements per 128-column row
+        const int col = (c & 15) * 8;
+        if (gi * kTileRows + r_in < a.m && gj * 128 + col < a.n) reg[i].template store<YT>(yt + r_in * a.sym + col, qs);
+      }
+    } else {
+      // Row groups: register i of thread t is chunk t % 16 of tile row
+      // 16 i + t / 16, so each row's amax reduces over 16 consecutive lanes.
+      const int col = (t & 15) * 8;
+#pragma unroll
+      for (int i = 0; i < CPT; ++i) {
+        uint32_t ra = reg[i].amax_bits();
+#pragma unroll
+        for (int off = 8; off > 0; off >>= 1) ra = max(ra, __shfl_xor_sync(0xffffffffu, ra, off));
+        const int64_t row = gi * kTileRows + i * 16 + (t >> 4);
+        const float safe = clamp_min_eps(__uint_as_float(ra), a.eps);
+        const float qs = quant_scale_from_amax(safe, fp8_max);
+        if (row < a.m) {
+          if ((t & 15) == 0) {
+            const float deq = (MODE == kDeqReciprocal) ? __frcp_rn(qs) : __fdiv_rn(safe, fp8_max);
+            a.scale[b * a.ssb + row * a.ssm + gj * a.ssn] = deq;
+          }
+          if (gj * 128 + col < a.n) reg[i].template store<YT>(yt + (i * 16 + (t >> 4)) * a.sym + col, qs);
+        }
+      }
     }
   }
   if (it < mine && t == 0) {
