@@ -551,6 +551,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                    ? __ldg(sb_b + (long long)g * p.ssbk + (long long)(col0 / p.qbn) * p.ssbn)
                    : 1.f;
       };
+      // Per-column scales (non-uniform B scales): lane l holds columns
+      // col0 + 32 q + l of the next K group.
+      float cnx[EPI_COLS / 32];
+      auto load_cols = [&](int g) {
+#pragma unroll
+        for (int q = 0; q < EPI_COLS / 32; ++q) {
+          const int c = col0 + q * 32 + lane;
+          cnx[q] = (sb_b && c < p.n && g < p.num_groups)
+                       ? __ldg(sb_b + (long long)g * p.ssbk + (long long)(c / p.qbn) * p.ssbn)
+                       : 1.f;
+        }
+      };
+      if constexpr (!COL_UNIFORM) load_cols(0);
       float rs[kScalePrefetch], cs[kScalePrefetch];
 #pragma unroll
       for (int j = 0; j < kScalePrefetch; ++j) {
@@ -571,14 +584,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             cs[j] = col_scale(g + kScalePrefetch);
           }
           if constexpr (!COL_UNIFORM) {
+            // Publish this group's column scales (loaded one group ahead) to
+            // the warp's shared slice, then start loading the next group's.
             __syncwarp();
 #pragma unroll
-            for (int i = lane; i < EPI_COLS; i += 32) {
-              const int c = col0 + i;
-              colscale[i] =
-                  (sb_b && c < p.n) ? __ldg(sb_b + (long long)g * p.ssbk + (long long)(c / p.qbn) * p.ssbn) : 1.f;
-            }
+            for (int q = 0; q < EPI_COLS / 32; ++q) colscale[q * 32 + lane] = cnx[q];
             __syncwarp();
+            load_cols(g + 1);
           }
           if (!wait(bar_tfull + 8 * abuf, aphase, SITE_GEMM_EPILOGUE)) {
             ok = false;
