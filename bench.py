@@ -287,7 +287,7 @@ def run_cfg5(args, world: int, rank: int, local_rank: int) -> None:
     from torch.distributed.fsdp import MixedPrecisionPolicy, fully_shard
 
     from practice_cuda_b200.fp8_linear import FP8BlockLinear
-    from practice_cuda_b200.fsdp_fp8 import enable_fp8_all_gather
+    from practice_cuda_b200.fsdp_fp8 import enable_fp8_all_gather, precompute_fp8_block_weights
     from practice_cuda_b200.llama import Llama, LlamaConfig
 
     os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
@@ -322,6 +322,8 @@ def run_cfg5(args, world: int, rank: int, local_rank: int) -> None:
         loss.backward()
         opt.step()
         opt.zero_grad(set_to_none=True)
+        if args.cfg5_linear == "fp8":
+            precompute_fp8_block_weights(model)  # quantize each shard once per step
         return loss
 
     for _ in range(args.warmup):

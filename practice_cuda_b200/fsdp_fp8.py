@@ -25,7 +25,7 @@ from typing import Any, Optional
 
 import torch
 import torch.nn as nn
-from torch.utils._pytree import tree_map_only
+from torch.utils._pytree import tree_flatten, tree_map_only
 
 from .fp8_linear import E4M3, BlockFP8Weight, FP8BlockLinear, quantize_weight
 
@@ -80,6 +80,12 @@ class FP8AllGatherWeight(torch.Tensor):
     @classmethod
     def __torch_dispatch__(cls, func, types, args=(), kwargs=None):
         kwargs = kwargs or {}
+        if func._schema.is_mutable:
+            # Any op that may write a weight (optimizer updates, FSDP's
+            # copy-in) invalidates its cached quantization.
+            for t in tree_flatten((args, kwargs))[0]:
+                if isinstance(t, FP8AllGatherWeight):
+                    t._mutations = getattr(t, "_mutations", 0) + 1
         args, kwargs = tree_map_only(FP8AllGatherWeight, lambda t: t._tensor, (args, kwargs))
         out = func(*args, **kwargs)
         if func not in _PRESERVE:
@@ -87,15 +93,17 @@ class FP8AllGatherWeight(torch.Tensor):
         return tree_map_only(torch.Tensor, FP8AllGatherWeight, out)
 
     # ---- FSDP2 all-gather extension -------------------------------------------
-    def fsdp_pre_all_gather(self, mesh, outer_size, outer_stride, module, mp_policy):
-        shard = self._tensor
-        if shard.shape[0] % 128 != 0:
-            raise ValueError(
-                f"per-block FP8 all-gather needs whole 128-row tiles per rank; shard has {shard.shape[0]} rows "
-                f"(out_features {outer_size[0]} over {mesh.size()} ranks)"
-            )
-        data, scale = quantize_weight(shard)
-        if mesh.size() == 1:
+    def _quantized_shard(self, world: int):
+        """All-gather inputs for the current shard values, cached until an
+        op that may write the weight runs on it (counted in
+        ``__torch_dispatch__``), so the backward re-gather and
+        :func:`precompute_fp8_block_weights` do not quantize twice."""
+        key = (getattr(self, "_mutations", 0), world)
+        cached = getattr(self, "_fp8_cache", None)
+        if cached is not None and cached[0] == key:
+            return self._fresh(cached[1], world), cached[2]
+        data, scale = quantize_weight(self._tensor.detach())
+        if world == 1:
             # FSDP2's single-rank path takes exactly one all-gather input, so
             # the scales ride in extra uint8 rows appended to the fp8 rows.
             rows, cols = data.shape
@@ -104,8 +112,26 @@ class FP8AllGatherWeight(torch.Tensor):
             packed = torch.zeros((rows + extra, cols), dtype=torch.uint8, device=data.device)
             packed[:rows].copy_(data.view(torch.uint8))
             packed[rows:].view(-1)[:sbytes].copy_(scale.reshape(-1).view(torch.uint8))
-            return (packed,), {"rows": rows, "scale_shape": tuple(scale.shape)}
-        return (data.view(torch.uint8), scale), None
+            inputs, meta = (packed,), {"rows": rows, "scale_shape": tuple(scale.shape)}
+        else:
+            inputs, meta = (data.view(torch.uint8), scale), None
+        self._fp8_cache = (key, inputs, meta)
+        return self._fresh(inputs, world), meta
+
+    @staticmethod
+    def _fresh(inputs, world):
+        # At world size 1 FSDP2 may use the all-gather input itself as the
+        # unsharded storage and free it on reshard: hand it a copy.
+        return tuple(t.clone() for t in inputs) if world == 1 else inputs
+
+    def fsdp_pre_all_gather(self, mesh, outer_size, outer_stride, module, mp_policy):
+        shard = self._tensor
+        if shard.shape[0] % 128 != 0:
+            raise ValueError(
+                f"per-block FP8 all-gather needs whole 128-row tiles per rank; shard has {shard.shape[0]} rows "
+                f"(out_features {outer_size[0]} over {mesh.size()} ranks)"
+            )
+        return self._quantized_shard(mesh.size())
 
     def fsdp_post_all_gather(
         self,
@@ -133,6 +159,31 @@ class FP8AllGatherWeight(torch.Tensor):
             out._scale = scale
             return None
         return BlockFP8Weight(data, scale, param_dtype), inner
+
+
+@torch.no_grad()
+def precompute_fp8_block_weights(module: nn.Module) -> int:
+    """Quantize every FP8 all-gather weight shard of ``module`` now.
+
+    Call after ``optimizer.step()``: the next FSDP2 unshard (and the backward
+    re-gather) then only copies the cached fp8 bytes and scales.  The
+    per-block counterpart of the reference's
+    ``precompute_bmm_float8_dynamic_scale_for_fsdp``
+    (``fp8_training/fp8_bench/modules/bmm_linear.py:676-752``); per-block
+    scales are local to a 128x128 tile, so no all-reduce is involved.
+    Returns the number of shards quantized.
+    """
+    count = 0
+    for m in module.modules():
+        if not isinstance(m, FP8BlockLinear):
+            continue
+        w = m.weight
+        local = getattr(w, "_local_tensor", w)  # DTensor shard under FSDP2
+        if isinstance(local, FP8AllGatherWeight):
+            mesh = getattr(w, "device_mesh", None)
+            local._quantized_shard(mesh.size() if mesh is not None else 1)
+            count += 1
+    return count
 
 
 def enable_fp8_all_gather(module: nn.Module) -> nn.Module:

@@ -17,6 +17,15 @@ def _free_port():
         return s.getsockname()[1]
 
 
+def distribute_like(param, full):
+    """``full`` laid out like the (possibly sharded) parameter."""
+    from torch.distributed.tensor import DTensor, distribute_tensor
+
+    if isinstance(param, DTensor):
+        return distribute_tensor(full, param.device_mesh, param.placements)
+    return full
+
+
 def _worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
     import torch.distributed as dist
@@ -28,7 +37,13 @@ def _worker(rank, world, port, q):
 
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        ff.quantize_weight = lambda w: oracle.per_block_quant(w, block_m=128, block_n=128)
+        calls = []
+
+        def counting_quant(w):
+            calls.append(1)
+            return oracle.per_block_quant(w, block_m=128, block_n=128)
+
+        ff.quantize_weight = counting_quant
         torch.manual_seed(0)
         full = torch.randn(512, 384) * 0.02
         m = torch.nn.Sequential(FP8BlockLinear(384, 512, bias=False))
@@ -48,9 +63,29 @@ def _worker(rank, world, port, q):
         FP8BlockLinear.forward = fwd
         for _ in range(2):  # first unshard and the re-gather into `out`
             m(torch.randn(2, 384))
-        ref_q, ref_s = oracle.per_block_quant(full, block_m=128, block_n=128)
-        ok = (seen["type"] is BlockFP8Weight and torch.equal(seen["data"], ref_q.view(torch.uint8))
-              and torch.equal(seen["scale"], ref_s))
+        def matches(w_full):
+            ref_q, ref_s = oracle.per_block_quant(w_full, block_m=128, block_n=128)
+            return (seen["type"] is BlockFP8Weight and torch.equal(seen["data"], ref_q.view(torch.uint8))
+                    and torch.equal(seen["scale"], ref_s))
+
+        ok = matches(full)
+        ok = ok and len(calls) == 1  # the re-gather reused the cached quantization
+        # An in-place update (what the optimizer does) invalidates the cache.
+        delta = torch.randn(512, 384, generator=torch.Generator().manual_seed(1)) * 0.01
+        m.reshard()  # the optimizer steps on sharded parameters
+        with torch.no_grad():
+            m[0].weight.add_(distribute_like(m[0].weight, delta))
+        w1 = m[0].weight.full_tensor()
+        m(torch.randn(2, 384))
+        ok = ok and matches(w1) and len(calls) == 2
+        # precompute after another update: the next unshard quantizes nothing.
+        m.reshard()
+        with torch.no_grad():
+            m[0].weight.add_(distribute_like(m[0].weight, delta))
+        w2 = m[0].weight.full_tensor()
+        ok = ok and ff.precompute_fp8_block_weights(m) == 1 and len(calls) == 3
+        m(torch.randn(2, 384))
+        ok = ok and matches(w2) and len(calls) == 3
         q.put((rank, bool(ok)))
     finally:
         dist.destroy_process_group()
