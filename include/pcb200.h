@@ -89,6 +89,19 @@ int pcb_quant_per_block(const void* x, int x_dtype, int64_t batch, int64_t m, in
                         int64_t block_m, int64_t block_n, float eps, void* stream);
 
 /*
+ * pcb_quant_per_block with power-of-two scales (E8M0 recipe of the per-block
+ * FP8 training linears; no counterpart in the reference, whose per-block
+ * scales are 1 / (448 / amax)).  Per block: r = RN(max(amax, eps) / fp8_max),
+ * e = smallest integer with 2^e >= r, y = fp8(x * 2^-e), scale = 2^e (fp32).
+ * Supported where x and y are contiguous along n with 16-byte aligned rows
+ * (PCB_ERR_UNSUPPORTED otherwise).  Same arguments as pcb_quant_per_block.
+ */
+int pcb_quant_per_block_pow2(const void* x, int x_dtype, int64_t batch, int64_t m, int64_t n, int64_t sxb,
+                             int64_t sxm, int64_t sxn, void* y, int y_dtype, int64_t syb, int64_t sym, int64_t syn,
+                             float* scale, int64_t ssb, int64_t ssm, int64_t ssn, int64_t block_m, int64_t block_n,
+                             float eps, void* stream);
+
+/*
  * Per-channel quantization.  Replaces triton_per_channel_quant
  * (fp8_training/fp8_bench/impls/triton_per_channel.py:90-219) and the torch
  * quantizer fp8_per_channel_quant_torch_compile

@@ -14,6 +14,7 @@ registry's ``QuantResult.dequantize``.
 from .quant import (  # noqa: F401
     FP8_MAX,
     per_block_quant,
+    per_block_quant_pow2,
     per_channel_quant,
     per_tensor_quant,
     legacy_per_tensor_quant,

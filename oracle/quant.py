@@ -71,6 +71,49 @@ def per_block_quant(
     return y, dequant_scale
 
 
+def per_block_quant_pow2(
+    x: torch.Tensor,
+    *,
+    block_m: int = 128,
+    block_n: int = 128,
+    fp8_dtype: torch.dtype = torch.float8_e4m3fn,
+    eps: float = 1e-12,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-block quantization with power-of-two (E8M0) scales.
+
+    Restates ``pcb_quant_per_block_pow2`` (the FP8 training recipe of this
+    library; the reference has no counterpart): ``r = RN(max(amax, eps) /
+    fp8_max)`` in fp32, ``e`` the smallest integer with ``2**e >= r`` (from
+    r's exponent and mantissa bits), ``quant_scale = 2**-e``, ``dequant =
+    1 / quant_scale``; a non-finite or subnormal ``r`` gives ``quant_scale =
+    1 / r``.  Tiles, tails and storage as :func:`per_block_quant`.
+    """
+    if x.ndim not in (2, 3):
+        raise ValueError(f"per-block quant expects a 2D or 3D tensor, got {tuple(x.shape)}")
+    squeeze = x.ndim == 2
+    xb = x.unsqueeze(0) if squeeze else x
+    batch, m, n = xb.shape
+    mb = (m + block_m - 1) // block_m
+    nb = (n + block_n - 1) // block_n
+    xf = torch.zeros((batch, mb * block_m, nb * block_n), dtype=torch.float32)
+    xf[:, :m, :n] = xb.float()
+    tiles = xf.view(batch, mb, block_m, nb, block_n)
+    safe = tiles.abs().amax(dim=(2, 4)).clamp_min(eps)
+    fp8_max = _fp8_max(fp8_dtype)
+    r = safe / fp8_max
+    bits = r.view(torch.int32)
+    ef = (bits >> 23) & 0xFF
+    e = ef - 127 + ((bits & 0x7FFFFF) != 0).to(torch.int32)
+    pow2 = ((127 - e).clamp(0, 254) << 23).view(torch.float32)
+    quant_scale = torch.where((ef == 0) | (ef == 0xFF), 1.0 / r, pow2)
+    dequant_scale = 1.0 / quant_scale
+    qs_full = quant_scale.repeat_interleave(block_m, dim=1).repeat_interleave(block_n, dim=2)
+    y = torch.clamp(xf * qs_full, min=-fp8_max, max=fp8_max)[:, :m, :n].to(fp8_dtype)
+    if squeeze:
+        return y[0], dequant_scale[0]
+    return y, dequant_scale
+
+
 def per_channel_quant(
     x: torch.Tensor,
     *,

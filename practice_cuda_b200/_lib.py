@@ -50,6 +50,11 @@ _SIGNATURES = {
         [_vp, _i, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _i64,
          _f, _vp],
     ),
+    "pcb_quant_per_block_pow2": (
+        _i,
+        [_vp, _i, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _i64,
+         _f, _vp],
+    ),
     "pcb_quant_per_channel": (
         _i,
         [_vp, _i, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i, _i64, _i64, _i64, _vp, _i64, _i64, _i, _f, _vp],

@@ -116,6 +116,8 @@ int launch_groups(const void* x, int xt, int64_t batch, int64_t m, int64_t n, in
       const dim3 grid((unsigned)((n + sw - 1) / sw), (unsigned)groups_m, (unsigned)batch);
       if (mode == quant::kDeqReciprocal)
         quant::quant_cols_cluster_kernel<XT, YT, true><<<grid, quant::kThreads, 0, stream>>>(a);
+      else if (mode == quant::kDeqPow2)
+        quant::quant_cols_cluster_kernel<XT, YT, true, quant::kDeqPow2><<<grid, quant::kThreads, 0, stream>>>(a);
       else
         return fail(PCB_ERR_UNSUPPORTED, "column-slab quantization is per-block only");
       return check_launch("quant_cols_cluster_kernel (slab)");
@@ -141,6 +143,10 @@ int launch_groups(const void* x, int xt, int64_t batch, int64_t m, int64_t n, in
         constexpr int YT = decltype(yc)::value;
         if constexpr (XT == PCB_DTYPE_BF16 || XT == PCB_DTYPE_F16) {
           constexpr int R = quant::kDeqReciprocal, D = quant::kDeqDivide;
+          constexpr int P = quant::kDeqPow2;
+          if (mode == P)
+            return gm == 1 ? go(quant::quant_tile128_tma_kernel<XT, YT, P, 1>, quant::TileCfg<1>{})
+                           : go(quant::quant_tile128_tma_kernel<XT, YT, P, 128>, quant::TileCfg<128>{});
           if (gm == 1)
             return mode == R ? go(quant::quant_tile128_tma_kernel<XT, YT, R, 1>, quant::TileCfg<1>{})
                              : go(quant::quant_tile128_tma_kernel<XT, YT, D, 1>, quant::TileCfg<1>{});
@@ -153,7 +159,7 @@ int launch_groups(const void* x, int xt, int64_t batch, int64_t m, int64_t n, in
     }
   }
   const int64_t cpg = gn / vec;
-  if (vec_ok && gm == 1 && cpg <= 32 && (32 % cpg) == 0) {
+  if (vec_ok && gm == 1 && cpg <= 32 && (32 % cpg) == 0 && mode != quant::kDeqPow2) {
     // Row groups of at most one warp (1x128 and narrower): contiguous row spans.
     constexpr int CH = 8;
     const int64_t spans_per_row = (n / vec + 32 * CH - 1) / (32 * CH);
@@ -201,6 +207,12 @@ int launch_groups(const void* x, int xt, int64_t batch, int64_t m, int64_t n, in
         kernel<<<(unsigned)grid, quant::kThreads, 0, stream>>>(a);
         return check_launch("quant_groups_kernel");
       };
+      if (mode == quant::kDeqPow2) {
+        if (nch <= 16) return go(quant::quant_groups_kernel<XT, YT, 8, 2, quant::kDeqPow2>, 8);
+        if (nch <= 32) return go(quant::quant_groups_kernel<XT, YT, 16, 2, quant::kDeqPow2>, 16);
+        if (nch <= 128) return go(quant::quant_groups_kernel<XT, YT, 32, 4, quant::kDeqPow2>, 32);
+        return go(quant::quant_groups_kernel<XT, YT, 256, 8, quant::kDeqPow2>, 256);
+      }
       if (mode == quant::kDeqReciprocal) {
         if (nch <= 16) return go(quant::quant_groups_kernel<XT, YT, 8, 2, quant::kDeqReciprocal>, 8);
         if (nch <= 32) return go(quant::quant_groups_kernel<XT, YT, 16, 2, quant::kDeqReciprocal>, 16);
@@ -214,6 +226,8 @@ int launch_groups(const void* x, int xt, int64_t batch, int64_t m, int64_t n, in
       }
     });
   }
+  if (mode == quant::kDeqPow2)
+    return fail(PCB_ERR_UNSUPPORTED, "power-of-two scales need x and y contiguous along n with 16-byte aligned rows");
   quant::GenericArgs a{x, sxb, sxm, sxn, y, syb, sym, syn, scale, ssb, ssm, ssn, batch, m, n, gm, gn,
                        groups_m, groups_n, num_groups, eps};
   return dispatch_xy(xt, yt, [&](auto xc, auto yc) -> int {
@@ -448,6 +462,19 @@ int pcb_quant_per_block(const void* x, int x_dtype, int64_t batch, int64_t m, in
   if (!is_float_in(x_dtype) || !is_fp8(y_dtype)) return fail(PCB_ERR_INVALID, "bad dtype");
   return launch_groups(x, x_dtype, batch, m, n, sxb, sxm, sxn, y, y_dtype, syb, sym, syn, scale, ssb, ssm, ssn,
                        block_m, block_n, quant::kDeqReciprocal, eps, (cudaStream_t)stream);
+}
+
+int pcb_quant_per_block_pow2(const void* x, int x_dtype, int64_t batch, int64_t m, int64_t n, int64_t sxb,
+                             int64_t sxm, int64_t sxn, void* y, int y_dtype, int64_t syb, int64_t sym, int64_t syn,
+                             float* scale, int64_t ssb, int64_t ssm, int64_t ssn, int64_t block_m, int64_t block_n,
+                             float eps, void* stream) {
+  if (batch < 0 || m < 0 || n < 0) return fail(PCB_ERR_INVALID, "negative size");
+  if (block_m <= 0 || block_n <= 0) return fail(PCB_ERR_INVALID, "block sizes must be positive");
+  if (batch * m * n == 0) return PCB_OK;
+  if (!x || !y || !scale) return fail(PCB_ERR_INVALID, "null pointer");
+  if (!is_float_in(x_dtype) || !is_fp8(y_dtype)) return fail(PCB_ERR_INVALID, "bad dtype");
+  return launch_groups(x, x_dtype, batch, m, n, sxb, sxm, sxn, y, y_dtype, syb, sym, syn, scale, ssb, ssm, ssn,
+                       block_m, block_n, quant::kDeqPow2, eps, (cudaStream_t)stream);
 }
 
 int pcb_quant_per_channel(const void* x, int x_dtype, int64_t batch, int64_t m, int64_t n, int64_t sxb, int64_t sxm,

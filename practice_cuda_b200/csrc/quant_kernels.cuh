@@ -18,7 +18,20 @@ constexpr int kThreads = 256;
 enum ScaleMode : int {
   kDeqReciprocal = 0,  // dequant = 1 / quant_scale     (per-block, per-tensor)
   kDeqDivide = 1,      // dequant = amax / fp8_max       (per-channel)
+  kDeqPow2 = 2,        // quant scale a power of two (E8M0), dequant = its reciprocal
 };
+
+template <int MODE>
+__device__ __forceinline__ float mode_quant_scale(float safe, float fp8_max) {
+  if constexpr (MODE == kDeqPow2) return pow2_quant_scale(safe, fp8_max);
+  else return quant_scale_from_amax(safe, fp8_max);
+}
+
+template <int MODE>
+__device__ __forceinline__ float mode_dequant_scale(float safe, float fp8_max, float qs) {
+  if constexpr (MODE == kDeqDivide) return __fdiv_rn(safe, fp8_max);
+  else return __frcp_rn(qs);
+}
 
 struct GroupArgs {
   const void* x;
@@ -177,9 +190,9 @@ __global__ void __launch_bounds__(kThreads) quant_groups_kernel(const GroupArgs 
     amax = team_max<TEAM>(amax, red);
 
     const float safe = clamp_min_eps(__uint_as_float(amax), args.eps);
-    const float qs = quant_scale_from_amax(safe, fp8_max);
+    const float qs = mode_quant_scale<MODE>(safe, fp8_max);
     if (active && t == 0) {
-      const float deq = (MODE == kDeqReciprocal) ? __frcp_rn(qs) : __fdiv_rn(safe, fp8_max);
+      const float deq = mode_dequant_scale<MODE>(safe, fp8_max, qs);
       args.scale[b * args.ssb + gi * args.ssm + gj * args.ssn] = deq;
     }
 #pragma unroll
@@ -352,7 +365,7 @@ struct ColArgs {
 //               rows split over a cluster, dequant = amax / fp8_max).
 // SLAB = true:  per-block (rows_per_cta x 1) blocks, e.g. 128 x 1: CTA
 //               blockIdx.y owns one row slab, dequant = 1 / quant_scale.
-template <int XT, int YT, bool SLAB = false>
+template <int XT, int YT, bool SLAB = false, int MODE = kDeqReciprocal>
 __global__ void __launch_bounds__(kThreads) quant_cols_cluster_kernel(const ColArgs args) {
   using C = Chunk<XT>;
   using T = typename C::T;
@@ -415,7 +428,7 @@ __global__ void __launch_bounds__(kThreads) quant_cols_cluster_kernel(const ColA
       for (int r = 0; r < nranks; ++r) v = max(v, cg::this_cluster().map_shared_rank(partial, r)[threadIdx.x]);
     }
     const float safe = clamp_min_eps(__uint_as_float(v), args.eps);
-    const float qs = quant_scale_from_amax(safe, fp8_max);
+    const float qs = SLAB ? mode_quant_scale<MODE>(safe, fp8_max) : quant_scale_from_amax(safe, fp8_max);
     qs_s[threadIdx.x] = qs;
     const int64_t c = col0 + threadIdx.x;
     if (SLAB && c < args.n) {

@@ -120,9 +120,9 @@ __global__ void __launch_bounds__(kThreads, TileCfg<GM>::CTAS_PER_SM)
 #pragma unroll
       for (int w = 0; w < kThreads / 32; ++w) r = max(r, red[it & 1][w]);
       const float safe = clamp_min_eps(__uint_as_float(r), a.eps);
-      const float qs = quant_scale_from_amax(safe, fp8_max);
+      const float qs = mode_quant_scale<MODE>(safe, fp8_max);
       if (t == 0) {
-        const float deq = (MODE == kDeqReciprocal) ? __frcp_rn(qs) : __fdiv_rn(safe, fp8_max);
+        const float deq = mode_dequant_scale<MODE>(safe, fp8_max, qs);
         a.scale[b * a.ssb + gi * a.ssm + gj * a.ssn] = deq;
       }
 #pragma unroll
@@ -143,10 +143,10 @@ __global__ void __launch_bounds__(kThreads, TileCfg<GM>::CTAS_PER_SM)
         for (int off = 8; off > 0; off >>= 1) ra = max(ra, __shfl_xor_sync(0xffffffffu, ra, off));
         const int64_t row = gi * kTileRows + i * 16 + (t >> 4);
         const float safe = clamp_min_eps(__uint_as_float(ra), a.eps);
-        const float qs = quant_scale_from_amax(safe, fp8_max);
+        const float qs = mode_quant_scale<MODE>(safe, fp8_max);
         if (row < a.m) {
           if ((t & 15) == 0) {
-            const float deq = (MODE == kDeqReciprocal) ? __frcp_rn(qs) : __fdiv_rn(safe, fp8_max);
+            const float deq = mode_dequant_scale<MODE>(safe, fp8_max, qs);
             a.scale[b * a.ssb + row * a.ssm + gj * a.ssn] = deq;
           }
           if (gj * 128 + col < a.n) reg[i].template store<YT>(yt + (i * 16 + (t >> 4)) * a.sym + col, qs);

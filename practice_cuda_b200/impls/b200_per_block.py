@@ -39,11 +39,15 @@ def b200_per_block_quant(
     fp8_dtype: torch.dtype = torch.float8_e4m3fn,
     eps: float = 1e-12,
     profile: bool = False,
+    pow2_scales: bool = False,
 ) -> QuantResult:
     """Per-block quantization (reference: triton_per_block_quant, :60-150).
 
     ``profile`` is accepted for signature compatibility; there is a single
-    static kernel configuration.
+    static kernel configuration.  ``pow2_scales`` selects the power-of-two
+    (E8M0) scales of the FP8 training recipe (pcb_quant_per_block_pow2; not
+    a reference option): every dequant scale is an exact power of two, which
+    the block-scaled tensor-core GEMM applies in hardware.
     """
     del profile
     if x.ndim not in {2, 3}:
@@ -65,14 +69,15 @@ def b200_per_block_quant(
     m_blocks = (m + block_m - 1) // block_m
     n_blocks = (n + block_n - 1) // block_n
     scale_storage = torch.empty((batch, m_blocks, n_blocks), device=x.device, dtype=torch.float32)
+    entry = "pcb_quant_per_block_pow2" if pow2_scales else "pcb_quant_per_block"
     _lib.check(
-        _lib.lib().pcb_quant_per_block(
+        getattr(_lib.lib(), entry)(
             x.data_ptr(), _lib.dtype_code(x.dtype), batch, m, n, sxb, x.stride(-2), x.stride(-1),
             output.data_ptr(), _lib.dtype_code(fp8_dtype), syb, output.stride(-2), output.stride(-1),
             scale_storage.data_ptr(), *scale_storage.stride(), block_m, block_n, eps,
             _lib.stream_ptr(x.device),
         ),
-        "pcb_quant_per_block",
+        entry,
     )
     dequant_scale = scale_storage.squeeze(0) if x.ndim == 2 else scale_storage
     return QuantResult(
@@ -85,6 +90,7 @@ def b200_per_block_quant(
             "fp8_dtype": str(fp8_dtype),
             "block_m": block_m,
             "block_n": block_n,
+            **({"scale_format": "e8m0"} if pow2_scales else {}),
         },
     )
 

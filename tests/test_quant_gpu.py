@@ -164,3 +164,24 @@ def test_dequantize_roundtrip_block():
     xh = q.dequantize().cpu()
     amax = x.float().abs().amax().item()
     assert torch.allclose(xh, x.float(), rtol=0.1, atol=0.05 * amax)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("shape,bm,bn", [
+    ((2, 300, 264), 1, 128),
+    ((2, 300, 264), 128, 128),
+    ((3, 384, 136), 128, 1),
+    ((257, 1024), 1, 128),
+])
+def test_per_block_pow2_vs_oracle(dtype, shape, bm, bn):
+    """Power-of-two (E8M0) scales of the training recipe: bytes and scales
+    bit-exact against the oracle restatement, every scale a power of two."""
+    x = synthetic(shape, outliers=True, seed=hash((shape, bm, bn, 2)) % 1000, dtype=dtype)
+    x[..., 0, :] = 0  # an all-zero row hits the eps clamp
+    q = get_quant("b200_per_block_2d").fn(x.to(DEV), block_m=bm, block_n=bn, pow2_scales=True)
+    y_ref, s_ref = oracle.per_block_quant_pow2(x, block_m=bm, block_n=bn)
+    assert_bytes_equal(q.tensor, y_ref, f"pow2 {shape} {bm}x{bn} {dtype}")
+    assert_scales_equal(q.dequant_scale, s_ref, f"pow2 {shape} {bm}x{bn} {dtype}")
+    s = q.dequant_scale.cpu()
+    assert torch.equal(torch.frexp(s).mantissa, torch.full_like(s, 0.5))
+    assert q.meta["scale_format"] == "e8m0"
