@@ -54,7 +54,7 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=["cfg3", "cfg5"], default="cfg3",
                     help="cfg3: per-block BMM step (default); cfg5: FSDP2 FP8 training step of the Llama decoder")
-    ap.add_argument("--cfg5-linear", choices=["fp8", "bf16"], default="fp8",
+    ap.add_argument("--cfg5-linear", choices=["fp8", "fp8_e8m0", "bf16"], default="fp8",
                     help="cfg5 only: per-block FP8 linears (default) or the bf16 baseline")
     ap.add_argument("--layers", type=int, default=8, help="cfg5 only: decoder layers (BASELINE: 8)")
     ap.add_argument("--fp8-peak", action="store_true",
@@ -295,7 +295,8 @@ def run_cfg5(args, world: int, rank: int, local_rank: int) -> None:
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     dist.init_process_group("nccl", device_id=device, rank=rank, world_size=world)
-    cfg = LlamaConfig(n_layers=args.layers)
+    cfg = LlamaConfig(n_layers=args.layers,
+                      linear_scaling="e8m0" if args.cfg5_linear == "fp8_e8m0" else "fp32")
     with torch.device(device):
         model = Llama(cfg)
     model.init_weights(seed=0)
@@ -322,7 +323,7 @@ def run_cfg5(args, world: int, rank: int, local_rank: int) -> None:
         loss.backward()
         opt.step()
         opt.zero_grad(set_to_none=True)
-        if args.cfg5_linear == "fp8":
+        if args.cfg5_linear != "bf16":
             precompute_fp8_block_weights(model)  # quantize each shard once per step
         return loss
 
@@ -353,12 +354,14 @@ def run_cfg5(args, world: int, rank: int, local_rank: int) -> None:
             "ms_per_step": ms,
             "higher_is_better": True,
             "scaling": "weak",
-            "dtype": "per-block e4m3 linears" if args.cfg5_linear == "fp8" else "bf16 linears",
+            "dtype": {"fp8": "per-block e4m3 linears (fp32 scales)",
+                      "fp8_e8m0": "per-block e4m3 linears (power-of-two scales, block-scaled MMA)",
+                      "bf16": "bf16 linears"}[args.cfg5_linear],
             "data": "synthetic token ids, random-init weights",
             "config": {"workload": "cfg5 FSDP2 training step", "layers": cfg.n_layers, "dim": cfg.dim,
                        "heads": cfg.n_heads, "ffn": cfg.ffn_dim, "vocab": cfg.vocab, "seq_len": cfg.seq_len,
                        "batch_per_gpu": 1, "parallelism": f"fsdp2 x{world}",
-                       "all_gather": "per-block fp8 + fp32 scales" if args.cfg5_linear == "fp8" else "bf16",
+                       "all_gather": "per-block fp8 + fp32 scales" if args.cfg5_linear != "bf16" else "bf16",
                        "lm_head_and_embedding": "bf16"},
             "linear_tflop_per_gpu_step": linear_flop / 1e12,
             "attention_tflop_per_gpu_step": attn_flop / 1e12,

@@ -196,6 +196,22 @@ int pcb_bmm_scaled(const void* a, int64_t sab, int64_t sam, int64_t sak,
                    int activation, void* stream);
 
 /*
+ * pcb_bmm_scaled for power-of-two scales (the E8M0 recipe of the per-block
+ * FP8 training linears, pcb_quant_per_block_pow2; no counterpart in the
+ * reference).  Same arguments; requires qbk == 128 and both scale tensors,
+ * and uses only the exponent bits of every scale (a scale that is not a
+ * power of two is truncated to 2^floor(log2)).  The tensor core applies the
+ * scales (tcgen05.mma.kind::mxf8f6f4.block_scale), so the fp32 accumulator
+ * stays in TMEM for the whole K loop.
+ */
+int pcb_bmm_block_scaled(const void* a, int64_t sab, int64_t sam, int64_t sak, const void* b, int64_t sbb,
+                         int64_t sbk, int64_t sbn, int ab_dtype, int64_t batch, int64_t m, int64_t n, int64_t k,
+                         const float* scale_a, int64_t ssab, int64_t ssam, int64_t ssak, int64_t qbm,
+                         const float* scale_b, int64_t ssbb, int64_t ssbk, int64_t ssbn, int64_t qbn, int64_t qbk,
+                         const void* bias, int bias_dtype, int64_t sbib, int64_t sbim, int64_t sbin, void* c,
+                         int c_dtype, int64_t scb, int64_t scm, int64_t scn, int activation, void* stream);
+
+/*
  * Fused quantize -> scaled FP8 GEMM (BASELINE cfg4).  The reference's fused
  * kernel (kernels/fp8_bmm/kernel/fp8_quant_bmm_fused_kernel.py:39-146) does not
  * run (SURVEY: produce_quant_scale is called with one argument and returns

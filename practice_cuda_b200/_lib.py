@@ -80,6 +80,18 @@ _SIGNATURES = {
          _vp, _i, _i64, _i64, _i64,  # c
          _i, _vp],
     ),
+    "pcb_bmm_block_scaled": (
+        _i,
+        [_vp, _i64, _i64, _i64,  # a
+         _vp, _i64, _i64, _i64, _i,  # b, ab dtype
+         _i64, _i64, _i64, _i64,  # batch m n k
+         _vp, _i64, _i64, _i64, _i64,  # scale a, strides, qbm
+         _vp, _i64, _i64, _i64, _i64,  # scale b, strides, qbn
+         _i64,  # qbk
+         _vp, _i, _i64, _i64, _i64,  # bias
+         _vp, _i, _i64, _i64, _i64,  # c
+         _i, _vp],
+    ),
     "pcb_quant_bmm_fused": (
         _i,
         [_vp, _i, _i64, _i64, _i64,  # x

@@ -13,6 +13,7 @@
 #include "gemm_sm100.cuh"
 #include "quant_kernels.cuh"
 #include "gemm_fused_sm100.cuh"
+#include "gemm_bs_sm100.cuh"
 #include "quant_tile_tma.cuh"
 
 using namespace pcb;
@@ -359,6 +360,38 @@ template <int BN, bool A_MN, bool B_MN, int FMT, bool PAIR>
 int launch_bmm_cols(const CUtensorMap& ta, const CUtensorMap& tb, const gemm::Params& p, int sm, cudaStream_t s) {
   if (p.col_uniform) return launch_bmm<BN, A_MN, B_MN, FMT, true, PAIR>(ta, tb, p, sm, s);
   return launch_bmm<BN, A_MN, B_MN, FMT, false, PAIR>(ta, tb, p, sm, s);
+}
+
+template <bool A_MN, bool B_MN, int FMT>
+int launch_bmm_bs(const CUtensorMap& ta, const CUtensorMap& tb, const gemm::Params& p, int sm_count,
+                  cudaStream_t stream) {
+  auto kernel = gemm::bmm_blockscaled_kernel<A_MN, B_MN, FMT>;
+  // Same setmaxnreg split as the 128x256 scaled kernel: launch only when
+  // ptxas allocated exactly the registers the split assumes.
+  static const int num_regs = [&] {
+    cudaFuncAttributes fa{};
+    return cudaFuncGetAttributes(&fa, kernel) == cudaSuccess ? fa.numRegs : -1;
+  }();
+  if (num_regs != gemm::kLaunchRegs)
+    return fail(PCB_ERR_UNSUPPORTED, "block-scaled bmm kernel register count differs from its setmaxnreg split");
+  ensure_smem_attr(kernel, gemm::BsSmem::ALLOC);
+  const int grid = std::min(p.num_tiles, sm_count);
+  kernel<<<grid, gemm::kThreads, gemm::BsSmem::ALLOC, stream>>>(ta, tb, p);
+  return check_launch("bmm_blockscaled_kernel");
+}
+
+int dispatch_bmm_bs(bool a_mn, bool b_mn, int fmt, const CUtensorMap& ta, const CUtensorMap& tb,
+                    const gemm::Params& p, int sm, cudaStream_t s) {
+  if (fmt == 0) {
+    if (!a_mn && !b_mn) return launch_bmm_bs<false, false, 0>(ta, tb, p, sm, s);
+    if (!a_mn && b_mn) return launch_bmm_bs<false, true, 0>(ta, tb, p, sm, s);
+    if (a_mn && !b_mn) return launch_bmm_bs<true, false, 0>(ta, tb, p, sm, s);
+    return launch_bmm_bs<true, true, 0>(ta, tb, p, sm, s);
+  }
+  if (!a_mn && !b_mn) return launch_bmm_bs<false, false, 1>(ta, tb, p, sm, s);
+  if (!a_mn && b_mn) return launch_bmm_bs<false, true, 1>(ta, tb, p, sm, s);
+  if (a_mn && !b_mn) return launch_bmm_bs<true, false, 1>(ta, tb, p, sm, s);
+  return launch_bmm_bs<true, true, 1>(ta, tb, p, sm, s);
 }
 
 template <int BN, bool PAIR>
@@ -717,12 +750,12 @@ int pcb_pack_u8(const void* src, int64_t batch, int64_t rows, int64_t cols, int6
   return check_launch("pack_u8_kernel");
 }
 
-int pcb_bmm_scaled(const void* a, int64_t sab, int64_t sam, int64_t sak, const void* b, int64_t sbb, int64_t sbk,
+static int bmm_entry(const void* a, int64_t sab, int64_t sam, int64_t sak, const void* b, int64_t sbb, int64_t sbk,
                    int64_t sbn, int ab_dtype, int64_t batch, int64_t m, int64_t n, int64_t k, const float* scale_a,
                    int64_t ssab, int64_t ssam, int64_t ssak, int64_t qbm, const float* scale_b, int64_t ssbb,
                    int64_t ssbk, int64_t ssbn, int64_t qbn, int64_t qbk, const void* bias, int bias_dtype,
                    int64_t sbib, int64_t sbim, int64_t sbin, void* c, int c_dtype, int64_t scb, int64_t scm,
-                   int64_t scn, int activation, void* stream) {
+                   int64_t scn, int activation, void* stream, bool block_scaled) {
   if (batch < 0 || m < 0 || n < 0 || k < 0) return fail(PCB_ERR_INVALID, "negative size");
   if (!is_fp8(ab_dtype)) return fail(PCB_ERR_INVALID, "A/B dtype must be E4M3 or E5M2");
   if (elem_size(c_dtype) == 0) return fail(PCB_ERR_INVALID, "bad output dtype");
@@ -751,7 +784,11 @@ int pcb_bmm_scaled(const void* a, int64_t sab, int64_t sam, int64_t sak, const v
   CUtensorMap ta, tb;
   // 128x256 tiles (128x128 when N <= 128): 32 KB of fp8 operands per
   // 128-deep K stage feed 8.4 MFLOP, which keeps L2 traffic per FLOP low.
-  const int bn = (n > 128) ? 256 : 128;
+  const int bn = (block_scaled || n > 128) ? 256 : 128;
+  if (block_scaled) {
+    if (!scale_a || !scale_b) return fail(PCB_ERR_INVALID, "block-scaled bmm needs both scale tensors");
+    if (qbk != gemm::BK) return fail(PCB_ERR_UNSUPPORTED, "block-scaled bmm needs qbk == 128");
+  }
   // 256x256 tiles on a CTA pair (cta_group::2) when M spans two 128-row
   // halves and the tile has a single K group (per-channel / per-tensor): each
   // CTA stages its own 128 A rows and half of the B tile.  With per-block
@@ -759,10 +796,10 @@ int pcb_bmm_scaled(const void* a, int64_t sab, int64_t sam, int64_t sak, const v
   // both CTAs' epilogues, which costs more across the pair than the smaller
   // B traffic saves, so those stay on one CTA.  PCB200_BMM_PAIR=0 turns the
   // pair off, =2 forces it on for per-block too (profiling knobs).
-  bool pair = bn == 256 && m > 128 && qbk >= k;
+  bool pair = !block_scaled && bn == 256 && m > 128 && qbk >= k;
   if (const char* e = std::getenv("PCB200_BMM_PAIR")) {
     const int v = std::atoi(e);
-    pair = (v == 2) ? (bn == 256 && m > 128) : (pair && v != 0);
+    pair = !block_scaled && ((v == 2) ? (bn == 256 && m > 128) : (pair && v != 0));
   }
   if (k == 0) {
     // No K stages: the kernel only writes bias/zeros; the maps are never read.
@@ -842,9 +879,31 @@ int pcb_bmm_scaled(const void* a, int64_t sab, int64_t sam, int64_t sak, const v
   if (const char* dbg = std::getenv("PCB200_BMM_DEBUG")) p.debug_flags = std::atoi(dbg);
   const int fmt = (ab_dtype == PCB_DTYPE_E4M3) ? 0 : 1;
   cudaStream_t s = (cudaStream_t)stream;
+  if (block_scaled) {
+    if (k == 0) return fail(PCB_ERR_UNSUPPORTED, "block-scaled bmm needs K > 0");
+    return dispatch_bmm_bs(a_mn, b_mn, fmt, ta, tb, p, di.sm_count, s);
+  }
   if (pair) return dispatch_bmm_layout<256, true>(a_mn, b_mn, fmt, ta, tb, p, di.sm_count, s);
   if (bn == 256) return dispatch_bmm_layout<256, false>(a_mn, b_mn, fmt, ta, tb, p, di.sm_count, s);
   return dispatch_bmm_layout<128, false>(a_mn, b_mn, fmt, ta, tb, p, di.sm_count, s);
 }
+int pcb_bmm_scaled(const void* a, int64_t sab, int64_t sam, int64_t sak, const void* b, int64_t sbb, int64_t sbk,
+                   int64_t sbn, int ab_dtype, int64_t batch, int64_t m, int64_t n, int64_t k, const float* scale_a,
+                   int64_t ssab, int64_t ssam, int64_t ssak, int64_t qbm, const float* scale_b, int64_t ssbb,
+                   int64_t ssbk, int64_t ssbn, int64_t qbn, int64_t qbk, const void* bias, int bias_dtype,
+                   int64_t sbib, int64_t sbim, int64_t sbin, void* c, int c_dtype, int64_t scb, int64_t scm,
+                   int64_t scn, int activation, void* stream) {
+  return bmm_entry(a, sab, sam, sak, b, sbb, sbk, sbn, ab_dtype, batch, m, n, k, scale_a, ssab, ssam, ssak, qbm, scale_b, ssbb, ssbk, ssbn, qbn, qbk, bias, bias_dtype, sbib, sbim, sbin, c, c_dtype, scb, scm, scn, activation, stream, false);
+}
+
+int pcb_bmm_block_scaled(const void* a, int64_t sab, int64_t sam, int64_t sak, const void* b, int64_t sbb, int64_t sbk,
+                         int64_t sbn, int ab_dtype, int64_t batch, int64_t m, int64_t n, int64_t k, const float* scale_a,
+                         int64_t ssab, int64_t ssam, int64_t ssak, int64_t qbm, const float* scale_b, int64_t ssbb,
+                         int64_t ssbk, int64_t ssbn, int64_t qbn, int64_t qbk, const void* bias, int bias_dtype,
+                         int64_t sbib, int64_t sbim, int64_t sbin, void* c, int c_dtype, int64_t scb, int64_t scm,
+                         int64_t scn, int activation, void* stream) {
+  return bmm_entry(a, sab, sam, sak, b, sbb, sbk, sbn, ab_dtype, batch, m, n, k, scale_a, ssab, ssam, ssak, qbm, scale_b, ssbb, ssbk, ssbn, qbn, qbk, bias, bias_dtype, sbib, sbim, sbin, c, c_dtype, scb, scm, scn, activation, stream, true);
+}
+
 
 }  // extern "C"

@@ -86,9 +86,10 @@ def dequantize_weight(data: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
     return data.float() * s
 
 
-def quantize_weight(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-    """(fp8 [out, in], fp32 [out/128, in/128]) -- 128x128 tiles."""
-    q = b200_per_block_quant(w, block_m=128, block_n=128)
+def quantize_weight(w: torch.Tensor, pow2: bool = False) -> tuple[torch.Tensor, torch.Tensor]:
+    """(fp8 [out, in], fp32 [out/128, in/128]) -- 128x128 tiles; ``pow2``
+    selects power-of-two (E8M0) scales."""
+    q = b200_per_block_quant(w, block_m=128, block_n=128, pow2_scales=pow2)
     return q.tensor, q.dequant_scale
 
 
@@ -96,8 +97,9 @@ def _as3(t: torch.Tensor) -> torch.Tensor:
     return t.unsqueeze(0)
 
 
-def _gemm(a, a_scale, a_strides, qbm, b, b_scale, b_strides, qbn, out_dtype):
-    """C[M, N] = sum_g (A_g B_g) sa sb with 128-deep K groups (2-D operands)."""
+def _gemm(a, a_scale, a_strides, qbm, b, b_scale, b_strides, qbn, out_dtype, block_scaled=False):
+    """C[M, N] = sum_g (A_g B_g) sa sb with 128-deep K groups (2-D operands);
+    ``block_scaled`` for power-of-two scales applied by the tensor core."""
     m = a.shape[0]
     n = b.shape[1]
     out = torch.empty((1, m, n), device=a.device, dtype=out_dtype)
@@ -105,21 +107,22 @@ def _gemm(a, a_scale, a_strides, qbm, b, b_scale, b_strides, qbn, out_dtype):
         _as3(a), _as3(b), out,
         scale_a=a_scale, sa_strides=(0,) + a_strides, qbm=qbm,
         scale_b=b_scale, sb_strides=(0,) + b_strides, qbn=qbn,
-        qbk=128, bias=None, activation="none",
+        qbk=128, bias=None, activation="none", block_scaled=block_scaled,
     )[0]
 
 
 class _FP8BlockLinearFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x2d: torch.Tensor, weight: torch.Tensor, w_data, w_scale):
+    def forward(ctx, x2d: torch.Tensor, weight: torch.Tensor, w_data, w_scale, pow2: bool = False):
         # x2d [T, in] bf16; weight is the high-precision parameter (for its
         # grad) and (w_data, w_scale) its 128x128 quantization.
-        qx = b200_per_block_quant(x2d, block_m=1, block_n=128)  # [T, in], scales [T, in/128]
+        ctx.pow2 = pow2
+        qx = b200_per_block_quant(x2d, block_m=1, block_n=128, pow2_scales=pow2)  # [T, in], scales [T, in/128]
         # y[T, out] = qx @ w.T: B = w.T is K-major (w stored [out, in]).
         wt = w_data.t()
         ws = w_scale
         y = _gemm(qx.tensor, qx.dequant_scale, tuple(qx.dequant_scale.stride()), 1,
-                  wt, ws, (ws.stride(1), ws.stride(0)), 128, x2d.dtype)
+                  wt, ws, (ws.stride(1), ws.stride(0)), 128, x2d.dtype, pow2)
         ctx.save_for_backward(x2d, w_data, w_scale)
         ctx.w_dtype = weight.dtype
         return y
@@ -127,25 +130,35 @@ class _FP8BlockLinearFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy: torch.Tensor):
         x2d, w_data, w_scale = ctx.saved_tensors
+        pow2 = ctx.pow2
         dy = dy.contiguous()
         # dgrad: dx[T, in] = q(dy 1x128 along out) @ w  (w as [K=out, N=in], N-major)
-        qdy = b200_per_block_quant(dy, block_m=1, block_n=128)
+        qdy = b200_per_block_quant(dy, block_m=1, block_n=128, pow2_scales=pow2)
         dx = _gemm(qdy.tensor, qdy.dequant_scale, tuple(qdy.dequant_scale.stride()), 1,
-                   w_data, w_scale, tuple(w_scale.stride()), 128, x2d.dtype)
+                   w_data, w_scale, tuple(w_scale.stride()), 128, x2d.dtype, pow2)
         # wgrad: dw[out, in] = q(dy 128x1 along T).T @ q(x 128x1 along T)
-        qdy_t = b200_per_block_quant(dy, block_m=128, block_n=1)   # scales [T/128, out]
-        qx_t = b200_per_block_quant(x2d, block_m=128, block_n=1)   # scales [T/128, in]
+        qdy_t = b200_per_block_quant(dy, block_m=128, block_n=1, pow2_scales=pow2)   # scales [T/128, out]
+        qx_t = b200_per_block_quant(x2d, block_m=128, block_n=1, pow2_scales=pow2)   # scales [T/128, in]
         a = qdy_t.tensor.t()                                       # [out, T], M-major
         sa = qdy_t.dequant_scale                                   # [T/128, out] -> (m, kg)
         b = qx_t.tensor                                            # [T, in], N-major
         sb = qx_t.dequant_scale                                    # [T/128, in] -> (kg, n)
-        dw = _gemm(a, sa, (sa.stride(1), sa.stride(0)), 1, b, sb, tuple(sb.stride()), 1, ctx.w_dtype)
-        return dx, dw, None, None
+        dw = _gemm(a, sa, (sa.stride(1), sa.stride(0)), 1, b, sb, tuple(sb.stride()), 1, ctx.w_dtype, pow2)
+        return dx, dw, None, None, None
 
 
 class FP8BlockLinear(nn.Linear):
     """``nn.Linear`` whose forward, dgrad and wgrad run on the per-block FP8
-    kernels (bias, if any, is added in high precision)."""
+    kernels (bias, if any, is added in high precision).
+
+    ``scaling`` (attribute, default ``"fp32"``): ``"fp32"`` quantizes with the
+    reference's fp32 scales (``dequant = 1 / (448 / amax)``) and promotes each
+    128-deep K group in the GEMM epilogue; ``"e8m0"`` rounds every scale up
+    to a power of two so the tensor core applies it
+    (``pcb_bmm_block_scaled``) and the accumulator never leaves TMEM.
+    """
+
+    scaling: str = "fp32"
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         w = self.weight
@@ -153,20 +166,20 @@ class FP8BlockLinear(nn.Linear):
             w_data, w_scale = w._data, w._scale
         else:
             master = getattr(w, "_tensor", w)  # FP8AllGatherWeight outside FSDP: its plain tensor
-            w_data, w_scale = quantize_weight(master.detach())
+            w_data, w_scale = quantize_weight(master.detach(), pow2=self.scaling == "e8m0")
         w_hp = w
         shape = x.shape
         x2d = x.reshape(-1, shape[-1])
         if x2d.stride(-1) != 1:
             x2d = x2d.contiguous()
-        y = _FP8BlockLinearFn.apply(x2d, w_hp, w_data, w_scale)
+        y = _FP8BlockLinearFn.apply(x2d, w_hp, w_data, w_scale, self.scaling == "e8m0")
         y = y.reshape(*shape[:-1], y.shape[-1])
         if self.bias is not None:
             y = y + self.bias
         return y
 
 
-def convert_to_fp8_block_linear(module: nn.Module, *, skip=lambda name, m: False) -> nn.Module:
+def convert_to_fp8_block_linear(module: nn.Module, *, skip=lambda name, m: False, scaling: str = "fp32") -> nn.Module:
     """Swap every ``nn.Linear`` (except those ``skip`` selects) for an
     :class:`FP8BlockLinear` sharing its parameters (cf. the reference's
     ``convert_to_float8_bmm_training``, ``modules/bmm_linear.py:661-673``)."""
@@ -177,7 +190,8 @@ def convert_to_fp8_block_linear(module: nn.Module, *, skip=lambda name, m: False
             new.in_features, new.out_features = child.in_features, child.out_features
             new.weight = child.weight
             new.bias = child.bias
+            new.scaling = scaling
             setattr(module, name, new)
         else:
-            convert_to_fp8_block_linear(child, skip=skip)
+            convert_to_fp8_block_linear(child, skip=skip, scaling=scaling)
     return module

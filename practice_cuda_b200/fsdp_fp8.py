@@ -52,7 +52,7 @@ class FP8AllGatherWeight(torch.Tensor):
     """High-precision weight whose FSDP2 all-gather is per-block FP8."""
 
     @staticmethod
-    def __new__(cls, tensor: torch.Tensor):
+    def __new__(cls, tensor: torch.Tensor, pow2: bool = False):
         return torch.Tensor._make_wrapper_subclass(
             cls,
             tensor.size(),
@@ -64,18 +64,19 @@ class FP8AllGatherWeight(torch.Tensor):
             requires_grad=tensor.requires_grad,
         )
 
-    def __init__(self, tensor: torch.Tensor):
+    def __init__(self, tensor: torch.Tensor, pow2: bool = False):
         self._tensor = tensor
+        self._pow2 = pow2  # power-of-two (E8M0) scales for the block-scaled GEMM
 
     def __repr__(self):
         return f"FP8AllGatherWeight({self._tensor!r})"
 
     def __tensor_flatten__(self):
-        return ["_tensor"], None
+        return ["_tensor"], {"pow2": self._pow2}
 
     @staticmethod
     def __tensor_unflatten__(inner, meta, outer_size, outer_stride):
-        return FP8AllGatherWeight(inner["_tensor"])
+        return FP8AllGatherWeight(inner["_tensor"], bool(meta and meta.get("pow2")))
 
     @classmethod
     def __torch_dispatch__(cls, func, types, args=(), kwargs=None):
@@ -86,11 +87,12 @@ class FP8AllGatherWeight(torch.Tensor):
             for t in tree_flatten((args, kwargs))[0]:
                 if isinstance(t, FP8AllGatherWeight):
                     t._mutations = getattr(t, "_mutations", 0) + 1
+        pow2 = any(t._pow2 for t in tree_flatten((args, kwargs))[0] if isinstance(t, FP8AllGatherWeight))
         args, kwargs = tree_map_only(FP8AllGatherWeight, lambda t: t._tensor, (args, kwargs))
         out = func(*args, **kwargs)
         if func not in _PRESERVE:
             return out
-        return tree_map_only(torch.Tensor, FP8AllGatherWeight, out)
+        return tree_map_only(torch.Tensor, lambda t: FP8AllGatherWeight(t, pow2), out)
 
     # ---- FSDP2 all-gather extension -------------------------------------------
     def _quantized_shard(self, world: int):
@@ -102,7 +104,8 @@ class FP8AllGatherWeight(torch.Tensor):
         cached = getattr(self, "_fp8_cache", None)
         if cached is not None and cached[0] == key:
             return self._fresh(cached[1], world), cached[2]
-        data, scale = quantize_weight(self._tensor.detach())
+        shard = self._tensor.detach()
+        data, scale = quantize_weight(shard, pow2=True) if self._pow2 else quantize_weight(shard)
         if world == 1:
             # FSDP2's single-rank path takes exactly one all-gather input, so
             # the scales ride in extra uint8 rows appended to the fp8 rows.
@@ -191,5 +194,6 @@ def enable_fp8_all_gather(module: nn.Module) -> nn.Module:
     FSDP2 all-gathers it as per-block FP8 (call before ``fully_shard``)."""
     for m in module.modules():
         if isinstance(m, FP8BlockLinear) and not isinstance(m.weight, FP8AllGatherWeight):
-            m.weight = nn.Parameter(FP8AllGatherWeight(m.weight.data), requires_grad=m.weight.requires_grad)
+            m.weight = nn.Parameter(FP8AllGatherWeight(m.weight.data, pow2=m.scaling == "e8m0"),
+                                    requires_grad=m.weight.requires_grad)
     return module

@@ -133,16 +133,20 @@ def bmm_scaled(
     qbk: int,
     bias: Optional[torch.Tensor],
     activation: str,
+    block_scaled: bool = False,
 ) -> torch.Tensor:
-    """Launch pcb_bmm_scaled; repack A/B to K-major once if TMA rejects them."""
+    """Launch pcb_bmm_scaled (pcb_bmm_block_scaled for power-of-two scales
+    applied by the tensor core); repack A/B to K-major once if TMA rejects them."""
     _lib.require_cuda(a, "A")
     batch, m, k = a.shape
     n = b.shape[-1]
     lib = _lib.lib()
     stream = _lib.stream_ptr(a.device)
 
+    entry = lib.pcb_bmm_block_scaled if block_scaled else lib.pcb_bmm_scaled
+
     def launch(a_t, b_t):
-        return lib.pcb_bmm_scaled(
+        return entry(
             a_t.data_ptr(), a_t.stride(0), a_t.stride(1), a_t.stride(2),
             b_t.data_ptr(), b_t.stride(0), b_t.stride(1), b_t.stride(2), _lib.dtype_code(a_t.dtype),
             batch, m, n, k,
@@ -159,5 +163,5 @@ def bmm_scaled(
     status = launch(a, b)
     if status == _lib.PCB_ERR_LAYOUT and k > 0:
         status = launch(pack_k_major(a, k_dim_last=True), pack_k_major(b, k_dim_last=False))
-    _lib.check(status, "pcb_bmm_scaled")
+    _lib.check(status, "pcb_bmm_block_scaled" if block_scaled else "pcb_bmm_scaled")
     return out

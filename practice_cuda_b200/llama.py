@@ -31,6 +31,7 @@ class LlamaConfig:
     seq_len: int = 4096
     norm_eps: float = 1e-5
     rope_theta: float = 10000.0
+    linear_scaling: str = "fp32"  # FP8BlockLinear.scaling: "fp32" or "e8m0"
 
     def linear_params(self) -> int:
         """Parameters in linear layers incl. the LM head (the FLOP basis)."""
@@ -79,6 +80,8 @@ class Block(nn.Module):
         self.w1 = FP8BlockLinear(d, f, bias=False)
         self.w3 = FP8BlockLinear(d, f, bias=False)
         self.w2 = FP8BlockLinear(f, d, bias=False)
+        for lin in (self.wq, self.wk, self.wv, self.wo, self.w1, self.w3, self.w2):
+            lin.scaling = cfg.linear_scaling
 
     def forward(self, x, cos, sin):
         b, t, d = x.shape
