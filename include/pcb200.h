@@ -200,7 +200,9 @@ int pcb_bmm_scaled(const void* a, int64_t sab, int64_t sam, int64_t sak,
  * FP8 training linears, pcb_quant_per_block_pow2; no counterpart in the
  * reference).  Same arguments; requires qbk == 128 and both scale tensors,
  * and uses only the exponent bits of every scale (a scale that is not a
- * power of two is truncated to 2^floor(log2)).  The tensor core applies the
+ * power of two is truncated to 2^floor(log2)).  The caller passes a device
+ * workspace of pcb_bmm_block_scaled_workspace_bytes() bytes, into which a
+ * pre-pass packs the scales in the layout the tensor core's scale copy reads.  The tensor core applies the
  * scales (tcgen05.mma.kind::mxf8f6f4.block_scale), so the fp32 accumulator
  * stays in TMEM for the whole K loop.
  */
@@ -209,7 +211,12 @@ int pcb_bmm_block_scaled(const void* a, int64_t sab, int64_t sam, int64_t sak, c
                          const float* scale_a, int64_t ssab, int64_t ssam, int64_t ssak, int64_t qbm,
                          const float* scale_b, int64_t ssbb, int64_t ssbk, int64_t ssbn, int64_t qbn, int64_t qbk,
                          const void* bias, int bias_dtype, int64_t sbib, int64_t sbim, int64_t sbin, void* c,
-                         int c_dtype, int64_t scb, int64_t scm, int64_t scn, int activation, void* stream);
+                         int c_dtype, int64_t scb, int64_t scm, int64_t scn, int activation, void* workspace,
+                         int64_t workspace_bytes, void* stream);
+
+/* Device workspace (bytes, 16-byte aligned) pcb_bmm_block_scaled needs for
+ * the packed E8M0 scale factors of both operands. */
+int64_t pcb_bmm_block_scaled_workspace_bytes(int64_t batch, int64_t m, int64_t n, int64_t k);
 
 /*
  * Fused quantize -> scaled FP8 GEMM (BASELINE cfg4).  The reference's fused

@@ -80,6 +80,7 @@ _SIGNATURES = {
          _vp, _i, _i64, _i64, _i64,  # c
          _i, _vp],
     ),
+    "pcb_bmm_block_scaled_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64]),
     "pcb_bmm_block_scaled": (
         _i,
         [_vp, _i64, _i64, _i64,  # a
@@ -90,8 +91,7 @@ _SIGNATURES = {
          _i64,  # qbk
          _vp, _i, _i64, _i64, _i64,  # bias
          _vp, _i, _i64, _i64, _i64,  # c
-         _i, _vp],
-    ),
+         _i, _vp, _i64, _vp]),
     "pcb_quant_bmm_fused": (
         _i,
         [_vp, _i, _i64, _i64, _i64,  # x

@@ -7,12 +7,13 @@
 // stays in TMEM for the whole K loop: no per-K-group promotion in registers.
 //
 // CTA = 12 warps, persistent over 128x256 output tiles (one CTA per SM):
-//   warp 0      TMA producer of the fp8 A / B stages (one elected lane, no multicast)
-//   warp 1      TMEM allocator + MMA issuer: per stage it copies the stage's
-//               scale factors from shared memory into TMEM (tcgen05.cp) and
-//               issues four block-scaled MMAs
-//   warp 2      scale-factor writer: converts the stage's fp32 power-of-two
-//               scales to E8M0 bytes in the 32x16-byte layout tcgen05.cp reads
+//   warp 0      producer: per stage one TMA load of A, one (or two) of B and
+//               bulk copies of the stage's packed E8M0 scale factors (1.5 KB,
+//               prepared by pack_sf_kernel in the 32 x 16-byte layout that
+//               tcgen05.cp reads); no multicast
+//   warp 1      TMEM allocator + MMA issuer: per stage it copies the scale
+//               factors from shared memory into TMEM (tcgen05.cp) and issues
+//               four block-scaled MMAs
 //   warps 4-11  epilogue (bias / GELU / cast / store), released as soon as the
 //               accumulator is in registers so the next tile's MMAs can start.
 #pragma once
@@ -78,6 +79,46 @@ constexpr uint32_t kBsTmemCols = 512;  // accumulator (256) + scale-factor ring
 // E8M0 byte of a power-of-two fp32 scale (its biased exponent).
 __device__ __forceinline__ uint32_t e8m0_of(float s) { return (__float_as_uint(s) >> 23) & 0xffu; }
 
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+// Packs the power-of-two fp32 scales of one operand into 512-byte blocks,
+// one per (batch, 128-row block, 128-deep K stage): line i (16 bytes) holds
+// the E8M0 bytes of rows i, i+32, i+64, i+96, each repeated for the four
+// 32-K blocks of the stage.  Rows past `rows` get 1.0 (byte 127).
+// scale(b, r, s) = scale[b * ssb + (r / qb) * ssr + s * sss].
+struct PackSfArgs {
+  const float* scale;
+  long long ssb, ssr, sss;
+  int qb;
+  int rows, row_blocks, k_stages, batch;
+  uint4* out;  // [batch][row_blocks][k_stages][32] lines
+};
+
+__global__ void __launch_bounds__(256) pack_sf_kernel(const PackSfArgs a) {
+  const long long total = (long long)a.batch * a.row_blocks * a.k_stages * 32;
+  for (long long idx = blockIdx.x * 256ll + threadIdx.x; idx < total; idx += (long long)gridDim.x * 256) {
+    const int i = (int)(idx & 31);
+    long long rest = idx >> 5;
+    const int ks = (int)(rest % a.k_stages);
+    rest /= a.k_stages;
+    const int rb = (int)(rest % a.row_blocks);
+    const int b = (int)(rest / a.row_blocks);
+    uint32_t w[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int r = rb * 128 + 32 * q + i;
+      const uint32_t e = r < a.rows ? e8m0_of(__ldg(a.scale + b * a.ssb + (long long)(r / a.qb) * a.ssr + ks * a.sss))
+                                    : 127u;
+      w[q] = e * 0x01010101u;
+    }
+    a.out[idx] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 template <bool A_MN, bool B_MN, int FMT>
 __global__ void __launch_bounds__(kThreads, 1)
     bmm_blockscaled_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -86,13 +127,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int BN = S::BN;
   constexpr int STAGES = S::STAGES;
   constexpr int EPI_COLS = BN / 2;
-  constexpr uint32_t STAGE_TX = S::A_BYTES + S::B_BYTES;
+  constexpr uint32_t STAGE_TX = S::A_BYTES + S::B_BYTES + S::SF_BYTES;
   static_assert(BN + STAGES * kSfCols <= (int)kBsTmemCols, "TMEM budget");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t s_base = smem_u32(smem);
-  const uint32_t bar_full = s_base + S::OFF_BAR;          // [STAGES]: TMA bytes + scale writer
+  const uint32_t bar_full = s_base + S::OFF_BAR;          // [STAGES]: operand + scale-factor bytes
   const uint32_t bar_empty = bar_full + 8 * STAGES;       // [STAGES]
   const uint32_t bar_tfull = bar_empty + 8 * STAGES;
   const uint32_t bar_tempty = bar_tfull + 8;
@@ -104,7 +145,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(bar_full + 8 * s, 2);
+      mbar_init(bar_full + 8 * s, 1);
       mbar_init(bar_empty + 8 * s, 1);
     }
     mbar_init(bar_tfull, 1);
@@ -152,6 +193,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else {
             tma_load_3d(sb_dst, &tmap_b, fb, ks * BK, nb * BN, b);
           }
+          const uint32_t sf_dst = s_base + S::OFF_SF + stage * S::SF_BYTES;
+          bulk_load(sf_dst, p.sfa + (((long long)b * p.m_blocks + mb) * p.k_stages + ks) * 32, 512, fb);
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+            bulk_load(sf_dst + 512 + 512 * j,
+                      p.sfb + (((long long)b * 2 * p.n_blocks + 2 * nb + j) * p.k_stages + ks) * 32, 512, fb);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -161,56 +208,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) {
         volatile int keep_waiting = 0;
         for (int s = 0; s < STAGES; ++s) mbar_wait_bounded(bar_full + 8 * s, 0, &keep_waiting, SITE_GEMM_PRODUCER);
-      }
-    } else if (warp == 2) {
-      // --------------------------- scale-factor writer ---------------------------
-      // Line i (16 bytes) of a 128-row block holds rows i, i+32, i+64, i+96;
-      // each row's 4 bytes are the E8M0 scales of its four 32-K blocks (all
-      // equal: one scale covers the stage's 128 K elements).
-      int stage = 0;
-      uint32_t phase = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-        const int b = tile / tiles_per_batch;
-        const int rem = tile - b * tiles_per_batch;
-        const int mb = rem / p.n_blocks;
-        const int nb = rem - mb * p.n_blocks;
-        const float* sa_b = p.sa + (long long)b * p.ssab;
-        const float* sb_b = p.sb + (long long)b * p.ssbb;
-        for (int ks = 0; ks < p.k_stages; ++ks) {
-          uint32_t w[12];
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int row = mb * BM + 32 * q + lane;
-            const uint32_t e =
-                row < p.m ? e8m0_of(__ldg(sa_b + (long long)(row / p.qbm) * p.ssam + (long long)ks * p.ssak)) : 127u;
-            w[q] = e * 0x01010101u;
-          }
-#pragma unroll
-          for (int j = 0; j < 2; ++j)
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const int col = nb * BN + 128 * j + 32 * q + lane;
-              const uint32_t e =
-                  col < p.n ? e8m0_of(__ldg(sb_b + (long long)ks * p.ssbk + (long long)(col / p.qbn) * p.ssbn)) : 127u;
-              w[4 + 4 * j + q] = e * 0x01010101u;
-            }
-          if (!mbar_wait_bounded(bar_empty + 8 * stage, phase ^ 1, abort_flag, SITE_GEMM_PRODUCER)) {
-            ok = false;
-            break;
-          }
-          uint8_t* sf = smem + S::OFF_SF + stage * S::SF_BYTES;
-          *reinterpret_cast<uint4*>(sf + lane * 16) = make_uint4(w[0], w[1], w[2], w[3]);
-          *reinterpret_cast<uint4*>(sf + 512 + lane * 16) = make_uint4(w[4], w[5], w[6], w[7]);
-          *reinterpret_cast<uint4*>(sf + 1024 + lane * 16) = make_uint4(w[8], w[9], w[10], w[11]);
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar_full + 8 * stage);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1;
-          }
-        }
       }
     } else if (warp == 1 && lane == 0) {
       // ------------------------------- MMA issuer -------------------------------

@@ -70,6 +70,9 @@ struct Params {
   float* xs;
   long long sxsb, sxsm, sxsk;
   float eps;
+  // Block-scaled GEMM only: packed E8M0 scale factors (pack_sf_kernel layout).
+  const uint4* sfa;
+  const uint4* sfb;
   int debug_flags;  // profiling only: 1 = epilogue skips its math, 2 = no MMAs issued, 4 = MMA ignores tmem-empty,
                    // 8 = fused quantizer skipped, 16 = no spin waits on a pair, 32 = spin waits on one CTA
 };

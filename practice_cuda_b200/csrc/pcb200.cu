@@ -750,12 +750,21 @@ int pcb_pack_u8(const void* src, int64_t batch, int64_t rows, int64_t cols, int6
   return check_launch("pack_u8_kernel");
 }
 
+int64_t pcb_bmm_block_scaled_workspace_bytes(int64_t batch, int64_t m, int64_t n, int64_t k) {
+  if (batch <= 0 || m <= 0 || n <= 0 || k <= 0) return 0;
+  const int64_t k_stages = (k + gemm::BK - 1) / gemm::BK;
+  const int64_t m_blocks = (m + gemm::BM - 1) / gemm::BM;
+  const int64_t n_blocks128 = 2 * ((n + 255) / 256);
+  return 512 * k_stages * batch * (m_blocks + n_blocks128);
+}
+
 static int bmm_entry(const void* a, int64_t sab, int64_t sam, int64_t sak, const void* b, int64_t sbb, int64_t sbk,
                    int64_t sbn, int ab_dtype, int64_t batch, int64_t m, int64_t n, int64_t k, const float* scale_a,
                    int64_t ssab, int64_t ssam, int64_t ssak, int64_t qbm, const float* scale_b, int64_t ssbb,
                    int64_t ssbk, int64_t ssbn, int64_t qbn, int64_t qbk, const void* bias, int bias_dtype,
                    int64_t sbib, int64_t sbim, int64_t sbin, void* c, int c_dtype, int64_t scb, int64_t scm,
-                   int64_t scn, int activation, void* stream, bool block_scaled) {
+                   int64_t scn, int activation, void* stream, bool block_scaled, void* workspace = nullptr,
+                     int64_t workspace_bytes = 0) {
   if (batch < 0 || m < 0 || n < 0 || k < 0) return fail(PCB_ERR_INVALID, "negative size");
   if (!is_fp8(ab_dtype)) return fail(PCB_ERR_INVALID, "A/B dtype must be E4M3 or E5M2");
   if (elem_size(c_dtype) == 0) return fail(PCB_ERR_INVALID, "bad output dtype");
@@ -881,6 +890,21 @@ static int bmm_entry(const void* a, int64_t sab, int64_t sam, int64_t sak, const
   cudaStream_t s = (cudaStream_t)stream;
   if (block_scaled) {
     if (k == 0) return fail(PCB_ERR_UNSUPPORTED, "block-scaled bmm needs K > 0");
+    const int64_t need = pcb_bmm_block_scaled_workspace_bytes(batch, m, n, k);
+    if (!workspace || workspace_bytes < need) return fail(PCB_ERR_INVALID, "block-scaled bmm workspace too small");
+    if (!aligned(workspace, 16)) return fail(PCB_ERR_INVALID, "block-scaled bmm workspace must be 16-byte aligned");
+    uint4* sfa = static_cast<uint4*>(workspace);
+    uint4* sfb = sfa + (int64_t)batch * p.m_blocks * p.k_stages * 32;
+    gemm::PackSfArgs pa{scale_a, ssab, ssam, ssak, p.qbm, (int)m, p.m_blocks, p.k_stages, (int)batch, sfa};
+    gemm::PackSfArgs pb{scale_b, ssbb, ssbn, ssbk, p.qbn, (int)n, 2 * p.n_blocks, p.k_stages, (int)batch, sfb};
+    for (const gemm::PackSfArgs& pk : {pa, pb}) {
+      const int64_t lines = (int64_t)pk.batch * pk.row_blocks * pk.k_stages * 32;
+      const unsigned grid = (unsigned)std::min<int64_t>((lines + 255) / 256, (int64_t)di.sm_count * 8);
+      gemm::pack_sf_kernel<<<grid, 256, 0, s>>>(pk);
+      if (int st = check_launch("pack_sf_kernel")) return st;
+    }
+    p.sfa = sfa;
+    p.sfb = sfb;
     return dispatch_bmm_bs(a_mn, b_mn, fmt, ta, tb, p, di.sm_count, s);
   }
   if (pair) return dispatch_bmm_layout<256, true>(a_mn, b_mn, fmt, ta, tb, p, di.sm_count, s);
@@ -901,8 +925,9 @@ int pcb_bmm_block_scaled(const void* a, int64_t sab, int64_t sam, int64_t sak, c
                          int64_t ssab, int64_t ssam, int64_t ssak, int64_t qbm, const float* scale_b, int64_t ssbb,
                          int64_t ssbk, int64_t ssbn, int64_t qbn, int64_t qbk, const void* bias, int bias_dtype,
                          int64_t sbib, int64_t sbim, int64_t sbin, void* c, int c_dtype, int64_t scb, int64_t scm,
-                         int64_t scn, int activation, void* stream) {
-  return bmm_entry(a, sab, sam, sak, b, sbb, sbk, sbn, ab_dtype, batch, m, n, k, scale_a, ssab, ssam, ssak, qbm, scale_b, ssbb, ssbk, ssbn, qbn, qbk, bias, bias_dtype, sbib, sbim, sbin, c, c_dtype, scb, scm, scn, activation, stream, true);
+                         int64_t scn, int activation, void* workspace,
+                         int64_t workspace_bytes, void* stream) {
+  return bmm_entry(a, sab, sam, sak, b, sbb, sbk, sbn, ab_dtype, batch, m, n, k, scale_a, ssab, ssam, ssak, qbm, scale_b, ssbb, ssbk, ssbn, qbn, qbk, bias, bias_dtype, sbib, sbim, sbin, c, c_dtype, scb, scm, scn, activation, stream, true, workspace, workspace_bytes);
 }
 
 

@@ -144,6 +144,11 @@ def bmm_scaled(
     stream = _lib.stream_ptr(a.device)
 
     entry = lib.pcb_bmm_block_scaled if block_scaled else lib.pcb_bmm_scaled
+    tail = (stream,)
+    if block_scaled:
+        ws_bytes = lib.pcb_bmm_block_scaled_workspace_bytes(batch, m, n, k)
+        workspace = torch.empty((max(ws_bytes, 16),), dtype=torch.uint8, device=a.device)
+        tail = (workspace.data_ptr(), ws_bytes, stream)
 
     def launch(a_t, b_t):
         return entry(
@@ -157,7 +162,7 @@ def bmm_scaled(
             _lib.dtype_code(bias.dtype) if bias is not None else 0,
             *(bias.stride() if bias is not None else (0, 0, 0)),
             out.data_ptr(), _lib.dtype_code(out.dtype), out.stride(0), out.stride(1), out.stride(2),
-            _lib.PCB_ACT[activation], stream,
+            _lib.PCB_ACT[activation], *tail,
         )
 
     status = launch(a, b)
