@@ -54,8 +54,9 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=["cfg3", "cfg5"], default="cfg3",
                     help="cfg3: per-block BMM step (default); cfg5: FSDP2 FP8 training step of the Llama decoder")
-    ap.add_argument("--cfg5-linear", choices=["fp8", "fp8_e8m0", "bf16"], default="fp8",
-                    help="cfg5 only: per-block FP8 linears (default) or the bf16 baseline")
+    ap.add_argument("--cfg5-linear", choices=["fp8_e8m0", "fp8", "bf16"], default="fp8_e8m0",
+                    help="cfg5 only: per-block FP8 linears with power-of-two scales on the block-scaled "
+                         "tensor-core GEMM (default), with the reference's fp32 scales (fp8), or the bf16 baseline")
     ap.add_argument("--layers", type=int, default=8, help="cfg5 only: decoder layers (BASELINE: 8)")
     ap.add_argument("--fp8-peak", action="store_true",
                     help="only measure the FP8 dense peak with torch._scaled_mm (cuBLASLt) at 8192^3")
