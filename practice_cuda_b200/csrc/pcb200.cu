@@ -91,6 +91,8 @@ int dispatch_xy(int xt, int yt, F&& f) {
 // ---------------------------------------------------------------------------
 bool make_map_x16(CUtensorMap* map, const void* base, int dt, uint64_t inner, uint64_t outer, uint64_t batch,
                   uint64_t outer_stride_bytes, uint64_t batch_stride_bytes);
+bool make_map_tile(CUtensorMap* map, const void* base, int dt, uint64_t inner, uint64_t outer, uint64_t batch,
+                   uint64_t outer_stride_bytes, uint64_t batch_stride_bytes);
 
 int launch_groups(const void* x, int xt, int64_t batch, int64_t m, int64_t n, int64_t sxb, int64_t sxm, int64_t sxn,
                   void* y, int yt, int64_t syb, int64_t sym, int64_t syn, float* scale, int64_t ssb, int64_t ssm,
@@ -124,12 +126,14 @@ int launch_groups(const void* x, int xt, int64_t batch, int64_t m, int64_t n, in
       return check_launch("quant_cols_cluster_kernel (slab)");
     });
   }
-  if (vec_ok && (gm == 128 || gm == 1) && gn == 128 && (xt == PCB_DTYPE_BF16 || xt == PCB_DTYPE_F16) &&
-      m <= INT32_MAX && n <= INT32_MAX && batch <= INT32_MAX) {
+  const bool tile16 = (xt == PCB_DTYPE_BF16 || xt == PCB_DTYPE_F16) && (gm == 128 || gm == 1);
+  const bool tile32 = xt == PCB_DTYPE_F32 && gm == 128;
+  if (vec_ok && (tile16 || tile32) && gn == 128 && m <= INT32_MAX && n <= INT32_MAX && batch <= INT32_MAX) {
     // 128x128 or 1x128 blocks of a 16-bit tensor: TMA-staged persistent kernel
     // over 128x128 tiles.
     CUtensorMap tm;
-    if (make_map_x16(&tm, x, xt, (uint64_t)n, (uint64_t)m, (uint64_t)batch, (uint64_t)sxm * 2, (uint64_t)sxb * 2)) {
+    const int es = elem_size(xt);
+    if (make_map_tile(&tm, x, xt, (uint64_t)n, (uint64_t)m, (uint64_t)batch, (uint64_t)sxm * es, (uint64_t)sxb * es)) {
       const int64_t num_tiles = batch * ((m + 127) / 128) * groups_n;
       quant::TileArgs a{y, syb, sym, scale, ssb, ssm, ssn, m, n, groups_m, groups_n, num_tiles, eps};
       auto go = [&](auto kernel, auto cfg) -> int {
@@ -142,7 +146,13 @@ int launch_groups(const void* x, int xt, int64_t batch, int64_t m, int64_t n, in
       return dispatch_xy(xt, yt, [&](auto xc, auto yc) -> int {
         constexpr int XT = decltype(xc)::value;
         constexpr int YT = decltype(yc)::value;
-        if constexpr (XT == PCB_DTYPE_BF16 || XT == PCB_DTYPE_F16) {
+        if constexpr (XT == PCB_DTYPE_F32) {
+          using Cfg = quant::TileCfg<128, 4>;
+          if (mode == quant::kDeqPow2) return go(quant::quant_tile128_tma_kernel<XT, YT, quant::kDeqPow2, 128>, Cfg{});
+          if (mode == quant::kDeqReciprocal)
+            return go(quant::quant_tile128_tma_kernel<XT, YT, quant::kDeqReciprocal, 128>, Cfg{});
+          return go(quant::quant_tile128_tma_kernel<XT, YT, quant::kDeqDivide, 128>, Cfg{});
+        } else if constexpr (XT == PCB_DTYPE_BF16 || XT == PCB_DTYPE_F16) {
           constexpr int R = quant::kDeqReciprocal, D = quant::kDeqDivide;
           constexpr int P = quant::kDeqPow2;
           if (mode == P)
@@ -301,6 +311,22 @@ bool make_map_x16(CUtensorMap* map, const void* base, int dt, uint64_t inner, ui
       dt == PCB_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   return fn(map, t, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Unswizzled (128, 128, 1) box of bf16 / fp16 / fp32 elements: one quantizer tile.
+bool make_map_tile(CUtensorMap* map, const void* base, int dt, uint64_t inner, uint64_t outer, uint64_t batch,
+                   uint64_t outer_stride_bytes, uint64_t batch_stride_bytes) {
+  if (dt != PCB_DTYPE_F32) return make_map_x16(map, base, dt, inner, outer, batch, outer_stride_bytes, batch_stride_bytes);
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {inner, outer, batch};
+  if (batch <= 1) batch_stride_bytes = std::max<uint64_t>(16, ((outer * outer_stride_bytes + 15) / 16) * 16);
+  cuuint64_t strides[2] = {outer_stride_bytes, batch_stride_bytes};
+  cuuint32_t box[3] = {128, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 

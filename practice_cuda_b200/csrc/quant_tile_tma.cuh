@@ -20,14 +20,16 @@ namespace pcb {
 namespace quant {
 
 constexpr int kTileRows = 128;
-constexpr int kTileBytes = 128 * 128 * 2;
+// Tile bytes for element size ES (2: bf16 / fp16; 4: fp32, 128x128 groups only).
+template <int ES>
+__host__ __device__ constexpr int tile_bytes() { return 128 * 128 * ES; }
 // 192 KB of tiles in flight per SM: one CTA of 6 stages for 128x128 groups;
 // 1x128 groups have more per-row work, so two CTAs of 3 stages share the SM.
-template <int GM>
+template <int GM, int ES = 2>
 struct TileCfg {
-  static constexpr int STAGES = (GM == 1) ? 2 : 6;
-  static constexpr int CTAS_PER_SM = 6 / STAGES;
-  static constexpr int SMEM = STAGES * kTileBytes + 1024 + 64;
+  static constexpr int STAGES = (GM == 1) ? 2 : (ES == 4 ? 3 : 6);
+  static constexpr int CTAS_PER_SM = (GM == 1) ? 3 : 1;
+  static constexpr int SMEM = STAGES * tile_bytes<ES>() + 1024 + 64;
 };
 
 struct TileArgs {
@@ -42,13 +44,17 @@ struct TileArgs {
 };
 
 template <int XT, int YT, int MODE, int GM>
-__global__ void __launch_bounds__(kThreads, TileCfg<GM>::CTAS_PER_SM)
+__global__ void __launch_bounds__(kThreads, TileCfg<GM, sizeof(typename InType<XT>::T)>::CTAS_PER_SM)
     quant_tile128_tma_kernel(const __grid_constant__ CUtensorMap tmap, const TileArgs a) {
-  static_assert(XT == PCB_DTYPE_BF16 || XT == PCB_DTYPE_F16, "16-bit inputs only");
+  static_assert(XT == PCB_DTYPE_BF16 || XT == PCB_DTYPE_F16 || (XT == PCB_DTYPE_F32 && GM == 128),
+                "16-bit inputs, or fp32 with 128x128 groups");
   static_assert(GM == 1 || GM == kTileRows, "whole-tile or per-row groups");
   using C = Chunk<XT>;
-  constexpr int kTileStages = TileCfg<GM>::STAGES;
-  constexpr int CPT = kTileBytes / 16 / kThreads;  // chunks per thread (8)
+  constexpr int ES = (int)sizeof(typename C::T);
+  constexpr int kTileBytes = tile_bytes<ES>();
+  constexpr int kTileStages = TileCfg<GM, ES>::STAGES;
+  constexpr int CPT = kTileBytes / 16 / kThreads;  // chunks per thread (8; 16 for fp32)
+  constexpr int CPR = 128 * ES / 16;               // 16-byte chunks per 128-column row
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t s_base = smem_u32(smem);
@@ -128,8 +134,8 @@ __global__ void __launch_bounds__(kThreads, TileCfg<GM>::CTAS_PER_SM)
 #pragma unroll
       for (int i = 0; i < CPT; ++i) {
         const int c = i * kThreads + t;
-        const int r_in = c >> 4;  // 16 chunks of 8 elements per 128-column row
-        const int col = (c & 15) * 8;
+        const int r_in = c / CPR;
+        const int col = (c % CPR) * C::VEC;
         if (gi * kTileRows + r_in < a.m && gj * 128 + col < a.n) reg[i].template store<YT>(yt + r_in * a.sym + col, qs);
       }
     } else {

@@ -53,7 +53,7 @@ def test_per_block_vs_oracle(dtype, shape, bm, bn):
     assert_scales_equal(q.dequant_scale, s_ref, f"{shape} {bm}x{bn} {dtype}")
 
 
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 def test_per_block_128x128_strided_rows_and_many_tiles(dtype):
     """128x128 tiles of a column-sliced view (row stride > n) and a tensor with
     many more tiles than SMs, so every CTA's staging ring wraps several times."""
