@@ -69,6 +69,17 @@ struct Chunk {
       return __half2float(__ushort_as_half((unsigned short)((i & 1) ? (w >> 16) : (w & 0xffffu))));
     }
   }
+  // 16-bit inputs: max |x| over the chunk as raw 16-bit magnitude bits
+  // (monotonic in |x| for bf16 and fp16, NaN above inf).
+  __device__ __forceinline__ uint32_t amax16() const {
+    const uint32_t m2 = __vmaxu2(__vmaxu2(raw.x & 0x7fff7fffu, raw.y & 0x7fff7fffu),
+                                 __vmaxu2(raw.z & 0x7fff7fffu, raw.w & 0x7fff7fffu));
+    return max(m2 & 0xffffu, m2 >> 16);
+  }
+  static __device__ __forceinline__ uint32_t bits16_to_f32_bits(uint32_t m) {
+    if constexpr (XT == PCB_DTYPE_BF16) return m << 16;
+    else return __float_as_uint(__half2float(__ushort_as_half((unsigned short)m)));
+  }
   // max |x| over the chunk as fp32 bits (NaN compares above +inf).
   __device__ __forceinline__ uint32_t amax_bits() const {
     if constexpr (XT == PCB_DTYPE_F32) {

@@ -141,12 +141,21 @@ __global__ void __launch_bounds__(kThreads, TileCfg<GM, sizeof(typename InType<X
     } else {
       // Row groups: register i of thread t is chunk t % 16 of tile row
       // 16 i + t / 16, so each row's amax reduces over 16 consecutive lanes.
+      // The 16-bit magnitudes of two registers share one word, so each
+      // shuffle step reduces two rows.
       const int col = (t & 15) * 8;
+      uint32_t rmax[CPT];
+#pragma unroll
+      for (int i = 0; i < CPT; i += 2) {
+        uint32_t w = reg[i].amax16() | (reg[i + 1].amax16() << 16);
+#pragma unroll
+        for (int off = 8; off > 0; off >>= 1) w = __vmaxu2(w, __shfl_xor_sync(0xffffffffu, w, off));
+        rmax[i] = C::bits16_to_f32_bits(w & 0xffffu);
+        rmax[i + 1] = C::bits16_to_f32_bits(w >> 16);
+      }
 #pragma unroll
       for (int i = 0; i < CPT; ++i) {
-        uint32_t ra = reg[i].amax_bits();
-#pragma unroll
-        for (int off = 8; off > 0; off >>= 1) ra = max(ra, __shfl_xor_sync(0xffffffffu, ra, off));
+        const uint32_t ra = rmax[i];
         const int64_t row = gi * kTileRows + i * 16 + (t >> 4);
         const float safe = clamp_min_eps(__uint_as_float(ra), a.eps);
         const float qs = mode_quant_scale<MODE>(safe, fp8_max);
