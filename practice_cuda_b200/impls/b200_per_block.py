@@ -190,22 +190,29 @@ def b200_per_block_bmm(
     out = check_out(out, batch, m, n, a_tensor.device, out_dtype)
     check_bias(bias, batch, m, n, a_tensor.device, require_n_contiguous=True)
     sa, sb = a.dequant_scale, b.dequant_scale
+    # Both operands with power-of-two (E8M0) scales and 128-deep K blocks: the
+    # tensor core applies the scales (pcb_bmm_block_scaled).
+    block_scaled = (a.meta.get("scale_format") == "e8m0" and b.meta.get("scale_format") == "e8m0"
+                    and expected_block_k == 128)
     return bmm_scaled(
         a_tensor, b_tensor, out,
         scale_a=sa, sa_strides=(sa.stride(0), sa.stride(1), sa.stride(2)), qbm=expected_block_m,
         scale_b=sb, sb_strides=(sb.stride(0), sb.stride(1), sb.stride(2)), qbn=expected_block_n,
-        qbk=expected_block_k, bias=bias, activation=activation,
+        qbk=expected_block_k, bias=bias, activation=activation, block_scaled=block_scaled,
     )
 
 
-def _register_block_scheme(quant_impl, *, a_block, b_block, description, register_quant_impl=True):
+def _register_block_scheme(quant_impl, *, a_block, b_block, description, register_quant_impl=True,
+                           pow2_scales=False):
     """Register one quant impl plus its five BMM layouts (reference :436-521)."""
     quant_a_kwargs = {"block_m": a_block[0], "block_n": a_block[1]}
     quant_b_kwargs = {"block_m": b_block[0], "block_n": b_block[1]}
+    if pow2_scales:
+        quant_a_kwargs["pow2_scales"] = quant_b_kwargs["pow2_scales"] = True
     if register_quant_impl:
         register_quant(
             quant_impl,
-            partial(b200_per_block_quant, block_m=a_block[0], block_n=a_block[1]),
+            partial(b200_per_block_quant, block_m=a_block[0], block_n=a_block[1], pow2_scales=pow2_scales),
             description,
         )
     common = {"quant_impl": quant_impl, "quant_a_kwargs": quant_a_kwargs, "quant_b_kwargs": quant_b_kwargs}

@@ -98,6 +98,7 @@ _BMM_QUANT_ORDER = {
     "b200_per_block_1d": 0,
     "b200_per_block_2d": 1,
     "b200_per_block_1x128_128x128": 2,
+    "b200_per_block_e8m0_1x128_128x128": 2,
     "b200_per_channel": 3,
     "b200_per_tensor": 4,
     "triton_per_block_1d": 5,

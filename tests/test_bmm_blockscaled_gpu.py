@@ -91,3 +91,20 @@ def test_fp8_linear_e8m0_forward_backward(t, din, dout):
     qdyt, sdyt = q(dy, block_m=128, block_n=1)
     qxt, sxt = q(x, block_m=128, block_n=1)
     assert_bmm_close(lin.weight.grad.float(), two_d(qdyt.t(), sdyt.t(), 1, qxt, sxt, 1), "wgrad")
+
+
+def test_registry_e8m0_scheme_runs_block_scaled():
+    """The registry scheme b200_per_block_e8m0_1x128_128x128 quantizes with
+    power-of-two scales and its BMM matches the promotion reference."""
+    from practice_cuda_b200 import get_bmm, get_quant
+
+    x = synthetic((2, 256, 384), outliers=True, seed=21)
+    w = synthetic((2, 384, 264), std=0.02, seed=22)
+    impl = get_bmm("b200_per_block_e8m0_1x128_128x128_a_k_b_n")
+    quant = get_quant(impl.quant_impl).fn
+    qa = quant(x.to(DEV), **impl.quant_a_kwargs)
+    qb = quant(w.to(DEV), **impl.quant_b_kwargs)
+    assert qa.meta["scale_format"] == "e8m0" and qb.meta["scale_format"] == "e8m0"
+    out = impl.fn(qa, qb)
+    ref = _ref(qa.tensor.cpu(), qa.dequant_scale.cpu(), 1, qb.tensor.cpu(), qb.dequant_scale.cpu(), 128)
+    assert_bmm_close(out, ref, "registry e8m0")

@@ -15,7 +15,7 @@ def test_reference_names_resolve():
                  "torch_compile_per_channel", "triton_per_channel_one_pass"]:
         assert get_quant(name).fn is not None
     for q in ["triton_per_block_1d", "triton_per_block_2d", "triton_per_channel", "triton_per_tensor",
-              "b200_per_block_1x128_128x128"]:
+              "b200_per_block_1x128_128x128", "b200_per_block_e8m0_1x128_128x128"]:
         for layout in ["a_k_b_k", "a_k_b_n", "a_k_b_n_transpose", "a_m_b_n", "a_m_transpose_b_n_transpose"]:
             impl = get_bmm(f"{q}_{layout}")
             assert impl.quant_impl == q
@@ -26,7 +26,7 @@ def test_reference_names_resolve():
 def test_bmm_name_order_groups_by_quant():
     names = bmm_impl_names()
     assert names[0].startswith("b200_per_block_1d")
-    assert len(names) == len(set(names)) == 5 * 9
+    assert len(names) == len(set(names)) == 5 * 10  # 9 quant schemes incl. the reference aliases + e8m0
 
 
 def test_duplicate_registration_rejected():
