@@ -137,6 +137,27 @@ int pcb_quant_per_tensor(const void* x, int x_dtype, int64_t batch, int64_t m, i
                          float fp8_max, float eps, float* workspace, void* stream);
 
 /*
+ * Dynamic float8 cast of the FP8 training linear.  Replaces the casts of
+ * hp_tensor_to_float8_dynamic (fp8_training/fp8_bench/modules/float8/
+ * float8_scaling_utils.py:29-72; amax_to_scale float8_utils.py:31-53,
+ * to_fp8_saturated :118-139) that Float8BMMLinear runs before every GEMM
+ * (modules/bmm_linear.py:229-310):
+ *   scale = fp8_max / max(amax, eps)  (fp32 IEEE divide: the reference's
+ *                                      float64 divide rounded to fp32 is the
+ *                                      same value), y = sat(fp8(x * scale)).
+ * The stored scale is this QUANT scale (Float8TrainingTensor._scale), not a
+ * dequant scale.  axiswise = 0: one scale for the whole tensor (tensorwise;
+ * `workspace` = pcb_quant_per_tensor_workspace_floats() floats, scale[0]);
+ * axiswise = 1: one scale per (batch, row), reduced over n (axiswise_dim=-1;
+ * scale[b*ssb + row*ssm], workspace unused).
+ */
+int pcb_quant_float8_dynamic(const void* x, int x_dtype, int64_t batch, int64_t m, int64_t n,
+                             int64_t sxb, int64_t sxm, int64_t sxn,
+                             void* y, int y_dtype, int64_t syb, int64_t sym, int64_t syn,
+                             float* scale, int64_t ssb, int64_t ssm, int axiswise, float eps,
+                             float* workspace, void* stream);
+
+/*
  * Per-tensor quantization that allocates nothing -- not even the small
  * workspace pcb_quant_per_tensor asks for.  No counterpart in the reference:
  * it exists for callers that cannot hand the library a scratch buffer, such
@@ -196,6 +217,24 @@ int pcb_bmm_scaled(const void* a, int64_t sab, int64_t sam, int64_t sak,
                    int activation, void* stream);
 
 /*
+ * pcb_bmm_scaled with A and B in different fp8 formats (a_dtype, b_dtype each
+ * E4M3 or E5M2), e.g. an E5M2 gradient times an E4M3 weight.  Replaces the
+ * mixed-format launches of the FP8 training linear's op
+ * fp8_bench::bmm_linear_tma (fp8_training/fp8_bench/modules/bmm_linear.py:121-227,
+ * called for dX and dW at :390-440 with E5M2 grad_output).  Other arguments as
+ * pcb_bmm_scaled.
+ */
+int pcb_bmm_scaled_mixed(const void* a, int64_t sab, int64_t sam, int64_t sak, int a_dtype,
+                         const void* b, int64_t sbb, int64_t sbk, int64_t sbn, int b_dtype,
+                         int64_t batch, int64_t m, int64_t n, int64_t k,
+                         const float* scale_a, int64_t ssab, int64_t ssam, int64_t ssak, int64_t qbm,
+                         const float* scale_b, int64_t ssbb, int64_t ssbk, int64_t ssbn, int64_t qbn,
+                         int64_t qbk,
+                         const void* bias, int bias_dtype, int64_t sbib, int64_t sbim, int64_t sbin,
+                         void* c, int c_dtype, int64_t scb, int64_t scm, int64_t scn,
+                         int activation, void* stream);
+
+/*
  * pcb_bmm_scaled for power-of-two scales (the E8M0 recipe of the per-block
  * FP8 training linears, pcb_quant_per_block_pow2; no counterpart in the
  * reference).  Same arguments; requires qbk == 128 and both scale tensors,
@@ -221,7 +260,7 @@ int64_t pcb_bmm_block_scaled_workspace_bytes(int64_t batch, int64_t m, int64_t n
 /*
  * Fused quantize -> scaled FP8 GEMM (BASELINE cfg4).  The reference's fused
  * kernel (kernels/fp8_bmm/kernel/fp8_quant_bmm_fused_kernel.py:39-146) does not
- * run (SURVEY: produce_quant_scale is called with one argument and returns
+ * run (its produce_quant_scale is called with one argument and returns
  * nothing); this is the working equivalent of what it intended:
  *   A = per-block 1x128 quantization of x (bf16/fp16, K contiguous) with the
  *       arithmetic of pcb_quant_per_block, done inside the GEMM;

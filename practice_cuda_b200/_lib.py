@@ -12,8 +12,7 @@ import threading
 
 import torch
 
-# PCB200_LIB points at another build of the same library (profiling variants only).
-LIB_PATH = os.environ.get("PCB200_LIB") or os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libpcb200.so")
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libpcb200.so")
 
 PCB_OK = 0
 PCB_ERR_INVALID = 1
@@ -60,6 +59,10 @@ _SIGNATURES = {
         [_vp, _i, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i, _i64, _i64, _i64, _vp, _i64, _i64, _i, _f, _vp],
     ),
     "pcb_quant_per_tensor_workspace_floats": (_i64, []),
+    "pcb_quant_float8_dynamic": (
+        _i,
+        [_vp, _i, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i, _i64, _i64, _i64, _vp, _i64, _i64, _i, _f, _vp, _vp],
+    ),
     "pcb_quant_per_tensor": (
         _i,
         [_vp, _i, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i, _i64, _i64, _i64, _vp, _vp, _i, _f, _f, _vp, _vp],
@@ -72,6 +75,18 @@ _SIGNATURES = {
         _i,
         [_vp, _i64, _i64, _i64,  # a
          _vp, _i64, _i64, _i64, _i,  # b, ab dtype
+         _i64, _i64, _i64, _i64,  # batch m n k
+         _vp, _i64, _i64, _i64, _i64,  # scale a, strides, qbm
+         _vp, _i64, _i64, _i64, _i64,  # scale b, strides, qbn
+         _i64,  # qbk
+         _vp, _i, _i64, _i64, _i64,  # bias
+         _vp, _i, _i64, _i64, _i64,  # c
+         _i, _vp],
+    ),
+    "pcb_bmm_scaled_mixed": (
+        _i,
+        [_vp, _i64, _i64, _i64, _i,  # a, a dtype
+         _vp, _i64, _i64, _i64, _i,  # b, b dtype
          _i64, _i64, _i64, _i64,  # batch m n k
          _vp, _i64, _i64, _i64, _i64,  # scale a, strides, qbm
          _vp, _i64, _i64, _i64, _i64,  # scale b, strides, qbn
@@ -117,6 +132,17 @@ class Pcb200Error(RuntimeError):
     def __init__(self, status: int, what: str, detail: str):
         self.status = status
         super().__init__(f"{what}: {status_name(status)}: {detail}")
+
+
+def use_library(path: str) -> None:
+    """Load another build of the same library (a ``PCB200_PROFILING`` build)
+    instead of the in-tree one.  Must be called before the first entry point
+    runs; for profiling and tests only."""
+    global LIB_PATH
+    with _lock:
+        if _lib is not None:
+            raise RuntimeError("libpcb200 is already loaded")
+        LIB_PATH = path
 
 
 def lib() -> ctypes.CDLL:

@@ -17,6 +17,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 SRC = os.path.join(HERE, "csrc", "pcb200.cu")
 OUT = os.path.join(HERE, "_lib", "libpcb200.so")
+PROF_OUT = os.path.join(HERE, "_lib", "libpcb200_prof.so")
 
 NVCC_FLAGS = [
     "-O3",
@@ -32,10 +33,10 @@ def _sources() -> list[str]:
     return sorted(glob.glob(os.path.join(HERE, "csrc", "*")) + glob.glob(os.path.join(ROOT, "include", "*.h")))
 
 
-def needs_build() -> bool:
-    if not os.path.exists(OUT):
+def needs_build(path: str = OUT) -> bool:
+    if not os.path.exists(path):
         return True
-    t = os.path.getmtime(OUT)
+    t = os.path.getmtime(path)
     return any(os.path.getmtime(s) > t for s in _sources())
 
 
@@ -46,23 +47,28 @@ def nvcc() -> str:
     return path
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    if not force and not needs_build():
-        return OUT
-    os.makedirs(os.path.dirname(OUT), exist_ok=True)
-    tmp = OUT + ".tmp"
-    cmd = [nvcc(), *NVCC_FLAGS, "-o", tmp, SRC]
+def build(force: bool = False, verbose: bool = False, profiling: bool = False, out: str | None = None) -> str:
+    """Build the library.  ``profiling`` compiles the PCB200_PROFILING
+    switches in (environment knobs that change kernel selection or skip work;
+    never shipped) into ``out`` (default ``_lib/libpcb200_prof.so``)."""
+    dst = out or (PROF_OUT if profiling else OUT)
+    if not force and not needs_build(dst):
+        return dst
+    os.makedirs(os.path.dirname(dst), exist_ok=True)
+    tmp = dst + ".tmp"
+    cmd = [nvcc(), *NVCC_FLAGS, *(["-DPCB200_PROFILING"] if profiling else []), "-o", tmp, SRC]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd), file=sys.stderr)
     subprocess.run(cmd, check=True)
-    os.replace(tmp, OUT)
-    return OUT
+    os.replace(tmp, dst)
+    return dst
 
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true")
+    ap.add_argument("--profiling", action="store_true", help="build libpcb200_prof.so with -DPCB200_PROFILING")
     args = ap.parse_args()
-    print(build(force=args.force, verbose=args.verbose))
+    print(build(force=args.force, verbose=args.verbose, profiling=args.profiling))

@@ -189,12 +189,16 @@ __device__ __forceinline__ float quant_scale_from_amax(float safe_amax, float fp
 
 // Power-of-two (E8M0) quantization scale: 2^-e with e the smallest integer
 // such that 2^e >= RN(safe_amax / fp8_max), so the dequant scale 2^e is exact
-// in an 8-bit exponent.  A non-finite or subnormal ratio r falls back to 1/r.
+// in an 8-bit exponent.  A zero or subnormal ratio r (eps = 0 and an all-zero
+// or tiny tile) is clamped up to the smallest normal power of two, 2^-126, so
+// its scale is still an E8M0 value; a non-finite r (inf / NaN input) gives
+// 1/r (0 or NaN), whose dequant scale (inf / NaN) packs to the E8M0 NaN byte.
 __device__ __forceinline__ float pow2_quant_scale(float safe_amax, float fp8_max) {
   const float r = __fdiv_rn(safe_amax, fp8_max);
   const uint32_t bits = __float_as_uint(r);
   const int ef = (int)((bits >> 23) & 0xffu);
-  if (ef == 0xff || ef == 0) return __frcp_rn(r);
+  if (ef == 0xff) return __frcp_rn(r);
+  if (ef == 0) return __uint_as_float((uint32_t)(127 + 126) << 23);  // 2^126
   const int e = ef - 127 + ((bits & 0x7fffffu) != 0u ? 1 : 0);
   return __uint_as_float((uint32_t)(127 - e) << 23);
 }

@@ -64,7 +64,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
   constexpr int EPI_COLS = S::EPI_COLS;
   constexpr int NACC = kNumAcc;
   constexpr uint32_t TMEM_COLS = NACC * BN;
-  constexpr uint32_t IDESC = make_idesc(BN, 0, 0, B_MN ? 1 : 0);
+  constexpr uint32_t IDESC = make_idesc(BN, 0, 0, 0, B_MN ? 1 : 0);
   constexpr uint32_t STAGE_TX = S::X_BYTES + S::B_BYTES;
   using C = quant::Chunk<XT>;
   static_assert(C::VEC == 8, "16-bit activations");
@@ -168,7 +168,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           for (int kk = 0; kk < BK / UMMA_K; ++kk) {
             const uint64_t a_off = (uint64_t)(kk * UMMA_K >> 4);
             const uint64_t b_off = B_MN ? (uint64_t)(kk * UMMA_K * 128 >> 4) : (uint64_t)(kk * UMMA_K >> 4);
-            if (!(p.debug_flags & 2)) umma_f8(d_tmem, adesc0 + a_off, bdesc0 + b_off, IDESC, kk > 0 ? 1u : 0u);
+            if (!(kProfiling && (p.debug_flags & 2))) umma_f8(d_tmem, adesc0 + a_off, bdesc0 + b_off, IDESC, kk > 0 ? 1u : 0u);
           }
           umma_commit(bar_empty + 8 * stage);
           umma_commit(bar_tfull + 8 * abuf);
@@ -205,7 +205,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         uint8_t* aq = smem + S::OFF_A + stage * S::A_BYTES;
         float* slot = ring + (gq % kScaleRing) * BM;
         const int kcol = ks * BK + c16 * 8;
-        if (!(p.debug_flags & 8)) {
+        if (!(kProfiling && (p.debug_flags & 8))) {
         // All 16 row-pair loads first (explicit shared-memory loads), then the
         // reductions and casts, so the loads overlap instead of serialising.
         const uint32_t xs_s = smem_u32(xs) + (uint32_t)(qw * 32 + half) * 256u + (uint32_t)c16 * 16u;
@@ -309,7 +309,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         }
         const float s_row = ring[slot * BM + row_in_tile];
         tc_fence_after();
-        if (p.debug_flags & 1) {
+        if (kProfiling && (p.debug_flags & 1)) {
           __syncwarp();
           if (lane == 0) mbar_arrive(bar_tempty + 8 * abuf);
           ++acc_cnt;

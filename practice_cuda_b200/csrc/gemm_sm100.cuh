@@ -5,7 +5,7 @@
 // CTA = 12 warps, persistent over output tiles (one CTA per SM):
 //   warp 0      TMA producer (one elected lane), no multicast
 //   warp 1      TMEM allocator + MMA issuer (one elected lane)
-//   warps 2-3   idle
+//   warps 2-3   idle (they only give their registers to the epilogue)
 //   warps 4-11  epilogue: two warpgroups; warpgroup h owns tile columns
 //               [h*BN/2, (h+1)*BN/2), warp (w % 4) owns TMEM lanes / rows
 //               [32*(w%4), 32*(w%4)+32).
@@ -13,8 +13,10 @@
 // buffers of BN fp32 columns, so the MMA of K-group g+1 runs while the
 // epilogue promotes group g.  With PAIR the tile is 256 x BN on a CTA pair
 // (cta_group::2): each CTA stages its own 128 A rows and half of the B
-// columns, the even CTA issues the MMAs for both and multicasts its commits,
-// and both CTAs' epilogues read their own TMEM half.
+// columns, the even CTA issues the MMAs for both and multicasts its commits
+// (smem stage free, accumulator full) to both CTAs, and both CTAs' epilogues
+// read their own TMEM half and arrive on the leader's accumulator-empty
+// barrier (plain remote arrives, no cluster-scope release).
 #pragma once
 
 #include "common.cuh"
@@ -39,8 +41,31 @@ static_assert(128 * kLowRegs + 256 * kHighRegs == kThreads * kLaunchRegs, "regis
 constexpr int kNumAcc = 4;        // TMEM accumulator buffers of BN fp32 columns
 constexpr int kScalePrefetch = 4;  // K groups of scales kept in flight per epilogue thread
 
+// Profiling switches (Params::debug_flags) exist only in builds compiled with
+// -DPCB200_PROFILING; the shipped library compiles every check below to false.
+#ifdef PCB200_PROFILING
+constexpr bool kProfiling = true;
+#else
+constexpr bool kProfiling = false;
+#endif
+
+// Cycle trace of CTA 0's pipeline hand-offs, compiled only into trace builds
+// (-DPCB_GEMM_TRACE) used to find where a K group's time goes.
+#ifdef PCB_GEMM_TRACE
+__device__ long long g_gemm_trace[16][1024];
+#define PCB_TRACE(ev, idx)                                                   \
+  do {                                                                       \
+    if (blockIdx.x == 0 && (idx) < 1024) g_gemm_trace[ev][idx] = clock64(); \
+  } while (0)
+#else
+#define PCB_TRACE(ev, idx) \
+  do {                     \
+  } while (0)
+#endif
+
 struct Params {
   int batch, m, n, k;
+  int a_fmt, b_fmt;  // operand formats for the instruction descriptor: 0 = E4M3, 1 = E5M2
   int m_blocks, n_blocks, num_tiles;
   int k_stages;          // ceil(k / BK)
   int stages_per_group;  // qbk / BK (or k_stages for a single group)
@@ -73,7 +98,7 @@ struct Params {
   // Block-scaled GEMM only: packed E8M0 scale factors (pack_sf_kernel layout).
   const uint4* sfa;
   const uint4* sfb;
-  int debug_flags;  // profiling only: 1 = epilogue skips its math, 2 = no MMAs issued, 4 = MMA ignores tmem-empty,
+  int debug_flags;  // PCB200_PROFILING builds only: 1 = epilogue skips its math, 2 = no MMAs issued, 4 = MMA ignores tmem-empty,
                    // 8 = fused quantizer skipped, 16 = no spin waits on a pair, 32 = spin waits on one CTA
 };
 
@@ -87,6 +112,14 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       "[%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
+}
+
+// L2 prefetch of one tensor-map box (no shared memory written, nothing to wait on).
+__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
 }
 
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
@@ -152,8 +185,11 @@ __device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap
       : "memory");
 }
 
+// Arrive on an mbarrier of another CTA of the cluster.  The TMEM reads this
+// publishes are ordered by tcgen05.fence::before_thread_sync, so no
+// cluster-scope release (a full memory fence) is needed.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
 }
 
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
@@ -211,6 +247,14 @@ __device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[1
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Ties registers filled by an earlier tcgen05.ld to a point after the
+// tcgen05.wait::ld, so the compiler cannot move their uses above the wait.
+template <int N>
+__device__ __forceinline__ void tmem_regs_ready(uint32_t (&r)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
+}
+
 // UMMA shared-memory descriptor for a 128-byte-swizzled tile.
 //   K-major : rows of 128 bytes (BK fp8), 8-row atoms 1024 B apart (SBO).
 //   MN-major: 128-element MN slabs, K rows 128 B apart; 8-K-row atoms 1024 B
@@ -225,9 +269,10 @@ __device__ __forceinline__ uint64_t make_sw128_desc(uint32_t saddr, uint32_t lbo
   return d;
 }
 
-// Instruction descriptor: fp32 accumulate, fp8 A/B, M=128, N=BN.
-__host__ __device__ constexpr uint32_t make_idesc(int bn, int ab_fmt, int a_mn, int b_mn, int m = BM) {
-  return (1u << 4) | ((uint32_t)ab_fmt << 7) | ((uint32_t)ab_fmt << 10) | ((uint32_t)a_mn << 15) |
+// Instruction descriptor of kind::f8f6f4: fp32 accumulate, A and B formats
+// (0 = E4M3, 1 = E5M2; they may differ), majorness, N = bn, M = m.
+__host__ __device__ constexpr uint32_t make_idesc(int bn, int a_fmt, int b_fmt, int a_mn, int b_mn, int m = BM) {
+  return (1u << 4) | ((uint32_t)a_fmt << 7) | ((uint32_t)b_fmt << 10) | ((uint32_t)a_mn << 15) |
          ((uint32_t)b_mn << 16) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
@@ -235,14 +280,22 @@ template <int BN, bool PAIR = false>
 struct Smem {
   // A CTA pair splits the B tile: each CTA stages BN/2 of its N rows.
   static constexpr int B_ROWS = PAIR ? BN / 2 : BN;
+#ifdef PCB_GEMM_PAIR_STAGES
+  static constexpr int STAGES = (BN == 256 && !PAIR) ? 4 : PCB_GEMM_PAIR_STAGES;
+#else
   static constexpr int STAGES = (BN == 256 && !PAIR) ? 4 : 6;
+#endif
   static constexpr int A_BYTES = BM * BK;      // 16 KB
   static constexpr int B_BYTES = B_ROWS * BK;  // 32 / 16 KB
   static constexpr int EPI_COLS = BN / 2;
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
   static constexpr int OFF_COLSCALE = OFF_B + STAGES * B_BYTES;           // 8 warps x EPI_COLS floats
+#ifdef PCB_GEMM_NO_COLSCALE
+  static constexpr int OFF_BAR = OFF_COLSCALE;
+#else
   static constexpr int OFF_BAR = OFF_COLSCALE + 8 * EPI_COLS * 4;
+#endif
   static constexpr int NUM_BARS = 2 * STAGES + 2 * kNumAcc;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;                  // tmem addr, abort flag
   static constexpr int BYTES = OFF_MISC + 16;
@@ -331,7 +384,7 @@ __device__ __forceinline__ void store_row(const Params& p, float* accf, int b, i
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, int AB_FMT, bool COL_UNIFORM, bool PAIR>
+template <int BN, bool A_MN, bool B_MN, bool COL_UNIFORM, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     bmm_scaled_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                       const Params p) {
@@ -342,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int NACC = (BN == 256) ? 2 : kNumAcc;
   constexpr uint32_t TMEM_COLS = NACC * BN;
   static_assert(NACC * BN <= 512, "TMEM holds 512 fp32 columns");
-  constexpr uint32_t IDESC = make_idesc(BN, AB_FMT, A_MN ? 1 : 0, B_MN ? 1 : 0, PAIR ? 2 * BM : BM);
+  const uint32_t IDESC = make_idesc(BN, p.a_fmt, p.b_fmt, A_MN ? 1 : 0, B_MN ? 1 : 0, PAIR ? 2 * BM : BM);
   // Bytes that land on the (leader's) full barrier per stage.
   constexpr uint32_t STAGE_TX = (PAIR ? 2 : 1) * (S::A_BYTES + S::B_BYTES);
   constexpr int TILE_M = PAIR ? 2 * BM : BM;  // output rows per tile
@@ -366,7 +419,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int first_tile = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
   // Waits whose arrival may come from the peer CTA poll without suspending
   // (flag 16 switches back to the suspending try_wait, profiling only).
-  const bool spin = (PAIR && !(p.debug_flags & 16)) || (p.debug_flags & 32);
+  const bool spin = (PAIR && !(kProfiling && (p.debug_flags & 16))) || (kProfiling && (p.debug_flags & 32));
   auto wait = [&](uint32_t bar, uint32_t parity, int site) -> bool {
     return spin ? mbar_spin_bounded(bar, parity, abort_flag, site) : mbar_wait_bounded(bar, parity, abort_flag, site);
   };
@@ -411,6 +464,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      // L2 prefetch cursor: the (tile, k stage) `pf_dist` stages ahead of the loads.
+      const int pf_dist = (kProfiling && (p.debug_flags & 64)) ? ((p.debug_flags >> 8) & 255) : 0;
+      int pf_tile = first_tile, pf_ks = 0;
+      int pcnt = 0;  // stages issued (trace index)
+      (void)pcnt;
+      auto pf_advance = [&]() {
+        if (++pf_ks == p.k_stages) {
+          pf_ks = 0;
+          pf_tile += tile_step;
+        }
+      };
+      auto pf_issue = [&]() {
+        if (pf_tile >= p.num_tiles) return;
+        const int pb = pf_tile / tiles_per_batch;
+        const int prem = pf_tile - pb * tiles_per_batch;
+        const int pmb = prem / p.n_blocks;
+        const int pnb = prem - pmb * p.n_blocks;
+        const int pa_row = pmb * TILE_M + (int)rank * BM;
+        const int pb_col = pnb * BN + (int)rank * S::B_ROWS;
+        if constexpr (A_MN) tma_prefetch_3d(&tmap_a, pa_row, pf_ks * BK, pb);
+        else tma_prefetch_3d(&tmap_a, pf_ks * BK, pa_row, pb);
+        if constexpr (B_MN) {
+#pragma unroll
+          for (int j = 0; j < S::B_ROWS / 128; ++j) tma_prefetch_3d(&tmap_b, pb_col + j * 128, pf_ks * BK, pb);
+        } else {
+          tma_prefetch_3d(&tmap_b, pf_ks * BK, pb_col, pb);
+        }
+      };
+      for (int i = 0; i < pf_dist; ++i) {
+        pf_issue();
+        pf_advance();
+      }
       for (int tile = first_tile; tile < p.num_tiles && ok; tile += tile_step) {
         const int b = tile / tiles_per_batch;
         const int rem = tile - b * tiles_per_batch;
@@ -419,10 +504,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int a_row = mb * TILE_M + (int)rank * BM;           // this CTA's A rows
         const int b_col = nb * BN + (int)rank * S::B_ROWS;        // this CTA's B columns
         for (int ks = 0; ks < p.k_stages; ++ks) {
+          if (pf_dist) {
+            pf_issue();
+            pf_advance();
+          }
+          PCB_TRACE(8, pcnt);
           if (!wait(bar_empty + 8 * stage, phase ^ 1, SITE_GEMM_PRODUCER)) {
             ok = false;
             break;
           }
+          PCB_TRACE(9, pcnt);
+          ++pcnt;
           const uint32_t fb = bar_full + 8 * stage;
           const uint32_t sa_dst = s_base + S::OFF_A + stage * S::A_BYTES;
           const uint32_t sb_dst = s_base + S::OFF_B + stage * S::B_BYTES;
@@ -470,10 +562,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int g = 0; g < p.num_groups && ok; ++g) {
           const uint32_t abuf = acc_cnt % NACC;
           const uint32_t aphase = (acc_cnt / NACC) & 1;
-          if (!(p.debug_flags & 4) && !wait(bar_tempty + 8 * abuf, aphase ^ 1, SITE_GEMM_MMA)) {
+          PCB_TRACE(0, acc_cnt);
+          if (!(kProfiling && (p.debug_flags & 4)) && !wait(bar_tempty + 8 * abuf, aphase ^ 1, SITE_GEMM_MMA)) {
             ok = false;
             break;
           }
+          PCB_TRACE(1, acc_cnt);
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + abuf * BN;
           const int ks0 = g * p.stages_per_group;
@@ -483,6 +577,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               ok = false;
               break;
             }
+            if (ks == ks0) PCB_TRACE(2, acc_cnt);
             tc_fence_after();
             const uint32_t sa_addr = s_base + S::OFF_A + stage * S::A_BYTES;
             const uint32_t sb_addr = s_base + S::OFF_B + stage * S::B_BYTES;
@@ -494,7 +589,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               // 32 rows of 128 bytes for an MN-major tile (encoded >> 4).
               const uint64_t a_off = A_MN ? (uint64_t)(kk * UMMA_K * 128 >> 4) : (uint64_t)(kk * UMMA_K >> 4);
               const uint64_t b_off = B_MN ? (uint64_t)(kk * UMMA_K * 128 >> 4) : (uint64_t)(kk * UMMA_K >> 4);
-              if (!(p.debug_flags & 2)) {
+              if (!(kProfiling && (p.debug_flags & 2))) {
                 if constexpr (PAIR) umma_f8_pair(d_tmem, adesc0 + a_off, bdesc0 + b_off, IDESC, (ks > ks0 || kk > 0) ? 1u : 0u);
                 else umma_f8(d_tmem, adesc0 + a_off, bdesc0 + b_off, IDESC, (ks > ks0 || kk > 0) ? 1u : 0u);
               }
@@ -511,6 +606,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // accumulator of group g ready (in both CTAs' TMEM)
           if constexpr (PAIR) umma_commit_pair(bar_tfull + 8 * abuf);
           else umma_commit(bar_tfull + 8 * abuf);
+          PCB_TRACE(3, acc_cnt);
           ++acc_cnt;
         }
       }
@@ -595,12 +691,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             load_cols(g + 1);
           }
+          if (threadIdx.x == 128) PCB_TRACE(4, acc_cnt);
           if (!wait(bar_tfull + 8 * abuf, aphase, SITE_GEMM_EPILOGUE)) {
             ok = false;
             break;
           }
+          if (threadIdx.x == 128) PCB_TRACE(5, acc_cnt);
           tc_fence_after();
-          if (p.debug_flags & 1) {
+          if (kProfiling && (p.debug_flags & 1)) {
             __syncwarp();
             if (lane == 0) {
               if constexpr (PAIR) mbar_arrive_cluster(bar_tempty_l + 8 * abuf);
@@ -616,6 +714,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int c = 0; c < EPI_COLS / 32; ++c) tmem_ld32_nowait(taddr + c * 32, v[c]);
             tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < EPI_COLS / 32; ++c) tmem_regs_ready(v[c]);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
@@ -636,44 +736,56 @@ __global__ void __launch_bounds__(kThreads, 1)
                                              s2, acc[c * 16 + i]);
               }
           } else {
-            // Wide half-tile: 16 columns at a time keeps the registers in budget.
+            // Wide half-tile: 16-column chunks; the TMEM load of chunk c+1 is
+            // in flight while chunk c is promoted, and the buffer is released
+            // as soon as the last chunk has landed in registers.
+            constexpr int CW = 16;
+            constexpr int NCH = EPI_COLS / CW;
+            uint32_t v[2][CW];
+            tmem_ld16_nowait(taddr, v[0]);
 #pragma unroll
-            for (int c = 0; c < EPI_COLS / 16; ++c) {
-              uint32_t v[16];
-              tmem_ld16_nowait(taddr + c * 16, v);
+            for (int c = 0; c < NCH; ++c) {
               tmem_wait_ld();
-#pragma unroll
+              tmem_regs_ready(v[c & 1]);
+              if (c + 1 < NCH) {
+                tmem_ld16_nowait(taddr + (c + 1) * CW, v[(c + 1) & 1]);
+              } else {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                  if constexpr (PAIR) mbar_arrive_cluster(bar_tempty_l + 8 * abuf);
+                  else mbar_arrive(bar_tempty + 8 * abuf);
+                }
+                if (threadIdx.x == 128) PCB_TRACE(6, acc_cnt);
+              }
+              const uint32_t* vc = v[c & 1];
               if constexpr (COL_UNIFORM) {
                 const float2 s2 = make_float2(s_row * s_col, s_row * s_col);
 #pragma unroll
-                for (int i = 0; i < 8; ++i)
-                  acc[c * 8 + i] = __ffma2_rn(make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])), s2,
-                                              acc[c * 8 + i]);
+                for (int i = 0; i < CW / 2; ++i)
+                  acc[c * (CW / 2) + i] = __ffma2_rn(
+                      make_float2(__uint_as_float(vc[2 * i]), __uint_as_float(vc[2 * i + 1])), s2, acc[c * (CW / 2) + i]);
               } else {
-                // 16 column scales of this chunk: four broadcast 16-byte shared loads.
+                // CW column scales of this chunk: broadcast 16-byte shared loads.
                 const float2 r2 = make_float2(s_row, s_row);
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
+                for (int q = 0; q < CW / 4; ++q) {
                   float4 cs4;
                   asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
                                : "=f"(cs4.x), "=f"(cs4.y), "=f"(cs4.z), "=f"(cs4.w)
-                               : "r"(colscale_s + (uint32_t)(c * 16 + 4 * q) * 4u));
+                               : "r"(colscale_s + (uint32_t)(c * CW + 4 * q) * 4u));
                   const float2 sa = __fmul2_rn(make_float2(cs4.x, cs4.y), r2);
                   const float2 sb2 = __fmul2_rn(make_float2(cs4.z, cs4.w), r2);
-                  acc[c * 8 + 2 * q] = __ffma2_rn(
-                      make_float2(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1])), sa, acc[c * 8 + 2 * q]);
-                  acc[c * 8 + 2 * q + 1] = __ffma2_rn(
-                      make_float2(__uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3])), sb2, acc[c * 8 + 2 * q + 1]);
+                  const int a0 = c * (CW / 2) + 2 * q;
+                  acc[a0] = __ffma2_rn(make_float2(__uint_as_float(vc[4 * q]), __uint_as_float(vc[4 * q + 1])), sa,
+                                       acc[a0]);
+                  acc[a0 + 1] = __ffma2_rn(make_float2(__uint_as_float(vc[4 * q + 2]), __uint_as_float(vc[4 * q + 3])),
+                                           sb2, acc[a0 + 1]);
                 }
               }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-              if constexpr (PAIR) mbar_arrive_cluster(bar_tempty_l + 8 * abuf);
-              else mbar_arrive(bar_tempty + 8 * abuf);
-            }
           }
+          if (threadIdx.x == 128) PCB_TRACE(7, acc_cnt);
           ++acc_cnt;
         }
       }

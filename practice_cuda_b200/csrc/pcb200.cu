@@ -128,7 +128,9 @@ int launch_groups(const void* x, int xt, int64_t batch, int64_t m, int64_t n, in
   }
   const bool tile16 = (xt == PCB_DTYPE_BF16 || xt == PCB_DTYPE_F16) && (gm == 128 || gm == 1);
   const bool tile32 = xt == PCB_DTYPE_F32 && gm == 128;
-  if (vec_ok && (tile16 || tile32) && gn == 128 && m <= INT32_MAX && n <= INT32_MAX && batch <= INT32_MAX) {
+  const bool quant_divide = mode == quant::kQuantDivide;  // dynamic float8 casts: group kernels only
+  if (vec_ok && (tile16 || tile32) && gn == 128 && m <= INT32_MAX && n <= INT32_MAX && batch <= INT32_MAX &&
+      !quant_divide) {
     // 128x128 or 1x128 blocks of a 16-bit tensor: TMA-staged persistent kernel
     // over 128x128 tiles.
     CUtensorMap tm;
@@ -170,7 +172,7 @@ int launch_groups(const void* x, int xt, int64_t batch, int64_t m, int64_t n, in
     }
   }
   const int64_t cpg = gn / vec;
-  if (vec_ok && gm == 1 && cpg <= 32 && (32 % cpg) == 0 && mode != quant::kDeqPow2) {
+  if (vec_ok && gm == 1 && cpg <= 32 && (32 % cpg) == 0 && mode != quant::kDeqPow2 && !quant_divide) {
     // Row groups of at most one warp (1x128 and narrower): contiguous row spans.
     constexpr int CH = 8;
     const int64_t spans_per_row = (n / vec + 32 * CH - 1) / (32 * CH);
@@ -224,6 +226,13 @@ int launch_groups(const void* x, int xt, int64_t batch, int64_t m, int64_t n, in
         if (nch <= 128) return go(quant::quant_groups_kernel<XT, YT, 32, 4, quant::kDeqPow2>, 32);
         return go(quant::quant_groups_kernel<XT, YT, 256, 8, quant::kDeqPow2>, 256);
       }
+      if (quant_divide) {
+        constexpr int Q = quant::kQuantDivide;
+        if (nch <= 16) return go(quant::quant_groups_kernel<XT, YT, 8, 2, Q>, 8);
+        if (nch <= 32) return go(quant::quant_groups_kernel<XT, YT, 16, 2, Q>, 16);
+        if (nch <= 128) return go(quant::quant_groups_kernel<XT, YT, 32, 4, Q>, 32);
+        return go(quant::quant_groups_kernel<XT, YT, 256, 8, Q>, 256);
+      }
       if (mode == quant::kDeqReciprocal) {
         if (nch <= 16) return go(quant::quant_groups_kernel<XT, YT, 8, 2, quant::kDeqReciprocal>, 8);
         if (nch <= 32) return go(quant::quant_groups_kernel<XT, YT, 16, 2, quant::kDeqReciprocal>, 16);
@@ -247,6 +256,8 @@ int launch_groups(const void* x, int xt, int64_t batch, int64_t m, int64_t n, in
     const int64_t grid = std::min<int64_t>(num_groups, (int64_t)di.sm_count * 8);
     if (mode == quant::kDeqReciprocal)
       quant::quant_groups_generic_kernel<XT, YT, quant::kDeqReciprocal><<<(unsigned)grid, quant::kThreads, 0, stream>>>(a);
+    else if (quant_divide)
+      quant::quant_groups_generic_kernel<XT, YT, quant::kQuantDivide><<<(unsigned)grid, quant::kThreads, 0, stream>>>(a);
     else
       quant::quant_groups_generic_kernel<XT, YT, quant::kDeqDivide><<<(unsigned)grid, quant::kThreads, 0, stream>>>(a);
     return check_launch("quant_groups_generic_kernel");
@@ -341,11 +352,11 @@ int launch_fused(const CUtensorMap& tx, const CUtensorMap& tb, const gemm::Param
 }
 
 
-template <int BN, bool A_MN, bool B_MN, int FMT, bool COLU, bool PAIR>
+template <int BN, bool A_MN, bool B_MN, bool COLU, bool PAIR>
 int launch_bmm(const CUtensorMap& ta, const CUtensorMap& tb, const gemm::Params& p, int sm_count,
                cudaStream_t stream) {
   using S = gemm::Smem<BN, PAIR>;
-  auto kernel = gemm::bmm_scaled_kernel<BN, A_MN, B_MN, FMT, COLU, PAIR>;
+  auto kernel = gemm::bmm_scaled_kernel<BN, A_MN, B_MN, COLU, PAIR>;
   if constexpr (BN == 256) {
     // This instantiation re-splits its registers with setmaxnreg; the split
     // is only valid when the launch holds exactly kLaunchRegs per thread
@@ -382,10 +393,10 @@ int launch_bmm(const CUtensorMap& ta, const CUtensorMap& tb, const gemm::Params&
   return check_launch("bmm_scaled_kernel");
 }
 
-template <int BN, bool A_MN, bool B_MN, int FMT, bool PAIR>
+template <int BN, bool A_MN, bool B_MN, bool PAIR>
 int launch_bmm_cols(const CUtensorMap& ta, const CUtensorMap& tb, const gemm::Params& p, int sm, cudaStream_t s) {
-  if (p.col_uniform) return launch_bmm<BN, A_MN, B_MN, FMT, true, PAIR>(ta, tb, p, sm, s);
-  return launch_bmm<BN, A_MN, B_MN, FMT, false, PAIR>(ta, tb, p, sm, s);
+  if (p.col_uniform) return launch_bmm<BN, A_MN, B_MN, true, PAIR>(ta, tb, p, sm, s);
+  return launch_bmm<BN, A_MN, B_MN, false, PAIR>(ta, tb, p, sm, s);
 }
 
 template <bool A_MN, bool B_MN, int FMT>
@@ -421,18 +432,12 @@ int dispatch_bmm_bs(bool a_mn, bool b_mn, int fmt, const CUtensorMap& ta, const 
 }
 
 template <int BN, bool PAIR>
-int dispatch_bmm_layout(bool a_mn, bool b_mn, int fmt, const CUtensorMap& ta, const CUtensorMap& tb,
-                        const gemm::Params& p, int sm, cudaStream_t s) {
-  if (fmt == 0) {
-    if (!a_mn && !b_mn) return launch_bmm_cols<BN, false, false, 0, PAIR>(ta, tb, p, sm, s);
-    if (!a_mn && b_mn) return launch_bmm_cols<BN, false, true, 0, PAIR>(ta, tb, p, sm, s);
-    if (a_mn && !b_mn) return launch_bmm_cols<BN, true, false, 0, PAIR>(ta, tb, p, sm, s);
-    return launch_bmm_cols<BN, true, true, 0, PAIR>(ta, tb, p, sm, s);
-  }
-  if (!a_mn && !b_mn) return launch_bmm_cols<BN, false, false, 1, PAIR>(ta, tb, p, sm, s);
-  if (!a_mn && b_mn) return launch_bmm_cols<BN, false, true, 1, PAIR>(ta, tb, p, sm, s);
-  if (a_mn && !b_mn) return launch_bmm_cols<BN, true, false, 1, PAIR>(ta, tb, p, sm, s);
-  return launch_bmm_cols<BN, true, true, 1, PAIR>(ta, tb, p, sm, s);
+int dispatch_bmm_layout(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const gemm::Params& p,
+                        int sm, cudaStream_t s) {
+  if (!a_mn && !b_mn) return launch_bmm_cols<BN, false, false, PAIR>(ta, tb, p, sm, s);
+  if (!a_mn && b_mn) return launch_bmm_cols<BN, false, true, PAIR>(ta, tb, p, sm, s);
+  if (a_mn && !b_mn) return launch_bmm_cols<BN, true, false, PAIR>(ta, tb, p, sm, s);
+  return launch_bmm_cols<BN, true, true, PAIR>(ta, tb, p, sm, s);
 }
 
 // ---------------------------------------------------------------------------
@@ -461,8 +466,11 @@ float* noalloc_partials_on_current_device() {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_partials);
     if (e != cudaSuccess || p == nullptr) {
-      g_last_error = std::string("pcb_quant_per_tensor_noalloc: cudaGetSymbolAddress failed: ") +
-                     cudaGetErrorString(e);
+      // Clear the pending (non-sticky) error so the next entry point's launch check
+      // does not report it as its own.
+      (void)cudaGetLastError();
+      fail(PCB_ERR_DEVICE, (std::string("pcb_quant_per_tensor_noalloc: cudaGetSymbolAddress failed: ") +
+                            cudaGetErrorString(e)).c_str());
       return nullptr;
     }
     addr[dev] = static_cast<float*>(p);
@@ -623,6 +631,47 @@ int pcb_quant_per_tensor(const void* x, int x_dtype, int64_t batch, int64_t m, i
   });
 }
 
+int pcb_quant_float8_dynamic(const void* x, int x_dtype, int64_t batch, int64_t m, int64_t n, int64_t sxb,
+                             int64_t sxm, int64_t sxn, void* y, int y_dtype, int64_t syb, int64_t sym, int64_t syn,
+                             float* scale, int64_t ssb, int64_t ssm, int axiswise, float eps, float* workspace,
+                             void* stream) {
+  if (batch < 0 || m < 0 || n < 0) return fail(PCB_ERR_INVALID, "negative size");
+  if (axiswise != 0 && axiswise != 1) return fail(PCB_ERR_INVALID, "axiswise must be 0 (tensorwise) or 1 (rows)");
+  if (!is_float_in(x_dtype) || !is_fp8(y_dtype)) return fail(PCB_ERR_INVALID, "bad dtype");
+  cudaStream_t s = (cudaStream_t)stream;
+  const float fp8_max = y_dtype == PCB_DTYPE_E4M3 ? 448.0f : 57344.0f;
+  if (axiswise) {
+    if (batch * m * n == 0) return PCB_OK;
+    if (!x || !y || !scale) return fail(PCB_ERR_INVALID, "null pointer");
+    return launch_groups(x, x_dtype, batch, m, n, sxb, sxm, sxn, y, y_dtype, syb, sym, syn, scale, ssb, ssm, 0, 1, n,
+                         quant::kQuantDivide, eps, s);
+  }
+  if (!x || !y || !scale || !workspace) return fail(PCB_ERR_INVALID, "null pointer");
+  const DeviceInfo di = device_info();
+  const int es = elem_size(x_dtype);
+  const int vec = 16 / es;
+  const bool vec_ok = sxn == 1 && syn == 1 && n % vec == 0 && aligned(x, 16) && (sxm * es) % 16 == 0 &&
+                      (batch == 1 || (sxb * es) % 16 == 0) && aligned(y, vec) && sym % vec == 0 &&
+                      (batch == 1 || syb % vec == 0);
+  const int64_t total = batch * m * n;
+  const int64_t per_cta = (int64_t)quant::kThreads * (vec_ok ? vec : 1);
+  const int amax_grid = (int)std::min<int64_t>(std::max<int64_t>(1, (total + per_cta - 1) / per_cta),
+                                               std::min<int64_t>((int64_t)di.sm_count * 4, quant::kPerTensorMaxPartials));
+  quant::TensorArgs a{x, sxb, sxm, sxn, y, syb, sym, syn, batch, m, n, vec_ok, workspace, amax_grid,
+                      scale, nullptr, PCB_DTYPE_F32, fp8_max, eps, 1};
+  return dispatch_xy(x_dtype, y_dtype, [&](auto xc, auto yc) -> int {
+    constexpr int XT = decltype(xc)::value;
+    constexpr int YT = decltype(yc)::value;
+    quant::tensor_amax_kernel<XT><<<amax_grid, quant::kThreads, 0, s>>>(a);
+    int st = check_launch("tensor_amax_kernel");
+    if (st != PCB_OK) return st;
+    const int cast_grid = (int)std::min<int64_t>(std::max<int64_t>(1, (total + per_cta - 1) / per_cta),
+                                                 (int64_t)di.sm_count * 8);
+    quant::tensor_cast_kernel<XT, YT><<<cast_grid, quant::kThreads, 0, s>>>(a);
+    return check_launch("tensor_cast_kernel");
+  });
+}
+
 int pcb_quant_per_tensor_noalloc(const void* x, int x_dtype, int64_t batch, int64_t m, int64_t n, int64_t sxb,
                                  int64_t sxm, int64_t sxn, void* y, int y_dtype, int64_t syb, int64_t sym,
                                  int64_t syn, float* quant_scale, float* dequant_scale, int scale_dtype,
@@ -746,8 +795,10 @@ int pcb_quant_bmm_fused(const void* x, int x_dtype, int64_t sxb, int64_t sxm, in
   p.sxsm = sxsm;
   p.sxsk = sxsk;
   p.eps = eps;
-  // Profiling knob: PCB200_BMM_DEBUG (1 epilogue math, 2 MMAs, 8 quantizer work skipped).
+#ifdef PCB200_PROFILING
+  // Profiling builds only: PCB200_BMM_DEBUG (1 epilogue math, 2 MMAs, 8 quantizer work skipped).
   if (const char* dbg = std::getenv("PCB200_BMM_DEBUG")) p.debug_flags = std::atoi(dbg);
+#endif
   cudaStream_t s = (cudaStream_t)stream;
   const int sm = di.sm_count;
   if (x_dtype == PCB_DTYPE_BF16) {
@@ -785,14 +836,17 @@ int64_t pcb_bmm_block_scaled_workspace_bytes(int64_t batch, int64_t m, int64_t n
 }
 
 static int bmm_entry(const void* a, int64_t sab, int64_t sam, int64_t sak, const void* b, int64_t sbb, int64_t sbk,
-                   int64_t sbn, int ab_dtype, int64_t batch, int64_t m, int64_t n, int64_t k, const float* scale_a,
+                   int64_t sbn, int ab_dtype, int b_dtype, int64_t batch, int64_t m, int64_t n, int64_t k,
+                   const float* scale_a,
                    int64_t ssab, int64_t ssam, int64_t ssak, int64_t qbm, const float* scale_b, int64_t ssbb,
                    int64_t ssbk, int64_t ssbn, int64_t qbn, int64_t qbk, const void* bias, int bias_dtype,
                    int64_t sbib, int64_t sbim, int64_t sbin, void* c, int c_dtype, int64_t scb, int64_t scm,
                    int64_t scn, int activation, void* stream, bool block_scaled, void* workspace = nullptr,
                      int64_t workspace_bytes = 0) {
   if (batch < 0 || m < 0 || n < 0 || k < 0) return fail(PCB_ERR_INVALID, "negative size");
-  if (!is_fp8(ab_dtype)) return fail(PCB_ERR_INVALID, "A/B dtype must be E4M3 or E5M2");
+  // ab_dtype is A's format; B's is b_dtype (the same unless the mixed entry point is used).
+  if (!is_fp8(ab_dtype) || !is_fp8(b_dtype)) return fail(PCB_ERR_INVALID, "A/B dtype must be E4M3 or E5M2");
+  if (block_scaled && ab_dtype != b_dtype) return fail(PCB_ERR_UNSUPPORTED, "block-scaled bmm needs one fp8 format");
   if (elem_size(c_dtype) == 0) return fail(PCB_ERR_INVALID, "bad output dtype");
   if (bias && !is_float_in(bias_dtype)) return fail(PCB_ERR_INVALID, "bias dtype must be F32/F16/BF16");
   if (activation != PCB_ACT_NONE && activation != PCB_ACT_GELU) return fail(PCB_ERR_INVALID, "bad activation");
@@ -824,18 +878,16 @@ static int bmm_entry(const void* a, int64_t sab, int64_t sam, int64_t sak, const
     if (!scale_a || !scale_b) return fail(PCB_ERR_INVALID, "block-scaled bmm needs both scale tensors");
     if (qbk != gemm::BK) return fail(PCB_ERR_UNSUPPORTED, "block-scaled bmm needs qbk == 128");
   }
-  // 256x256 tiles on a CTA pair (cta_group::2) when M spans two 128-row
-  // halves and the tile has a single K group (per-channel / per-tensor): each
-  // CTA stages its own 128 A rows and half of the B tile.  With per-block
-  // scales every K group is a TMEM round trip between the leader's MMA and
-  // both CTAs' epilogues, which costs more across the pair than the smaller
-  // B traffic saves, so those stay on one CTA.  PCB200_BMM_PAIR=0 turns the
-  // pair off, =2 forces it on for per-block too (profiling knobs).
-  bool pair = !block_scaled && bn == 256 && m > 128 && qbk >= k;
-  if (const char* e = std::getenv("PCB200_BMM_PAIR")) {
-    const int v = std::atoi(e);
-    pair = !block_scaled && ((v == 2) ? (bn == 256 && m > 128) : (pair && v != 0));
-  }
+  // 256x256 tiles on a CTA pair (cta_group::2) whenever M spans two 128-row
+  // halves: each CTA stages its own 128 A rows and half of the B tile, so an
+  // SM moves 32 KB of operands per 128-deep K stage instead of 48 KB.  Per-K-
+  // group promotion runs on both CTAs' epilogues, which hand each TMEM
+  // accumulator back to the leader's MMA issuer.
+  bool pair = !block_scaled && bn == 256 && m > 128;
+#ifdef PCB200_PROFILING
+  // Profiling builds only: PCB200_BMM_PAIR=0 keeps every tile on one CTA.
+  if (const char* e = std::getenv("PCB200_BMM_PAIR")) pair = pair && std::atoi(e) != 0;
+#endif
   if (k == 0) {
     // No K stages: the kernel only writes bias/zeros; the maps are never read.
     std::memset(&ta, 0, sizeof(ta));
@@ -909,10 +961,14 @@ static int bmm_entry(const void* a, int64_t sab, int64_t sam, int64_t sak, const
   p.bias_dtype = bias_dtype;
   p.activation = activation;
   p.inject_error = g_inject_error.exchange(0);
-  // Profiling knob (never set in production): PCB200_BMM_DEBUG=1 skips the
-  // epilogue math, =2 skips the MMAs; results are then meaningless.
+#ifdef PCB200_PROFILING
+  // Profiling builds only: PCB200_BMM_DEBUG=1 skips the epilogue math, =2
+  // skips the MMAs; results are then meaningless.
   if (const char* dbg = std::getenv("PCB200_BMM_DEBUG")) p.debug_flags = std::atoi(dbg);
+#endif
   const int fmt = (ab_dtype == PCB_DTYPE_E4M3) ? 0 : 1;
+  p.a_fmt = fmt;
+  p.b_fmt = (b_dtype == PCB_DTYPE_E4M3) ? 0 : 1;
   cudaStream_t s = (cudaStream_t)stream;
   if (block_scaled) {
     if (k == 0) return fail(PCB_ERR_UNSUPPORTED, "block-scaled bmm needs K > 0");
@@ -933,9 +989,9 @@ static int bmm_entry(const void* a, int64_t sab, int64_t sam, int64_t sak, const
     p.sfb = sfb;
     return dispatch_bmm_bs(a_mn, b_mn, fmt, ta, tb, p, di.sm_count, s);
   }
-  if (pair) return dispatch_bmm_layout<256, true>(a_mn, b_mn, fmt, ta, tb, p, di.sm_count, s);
-  if (bn == 256) return dispatch_bmm_layout<256, false>(a_mn, b_mn, fmt, ta, tb, p, di.sm_count, s);
-  return dispatch_bmm_layout<128, false>(a_mn, b_mn, fmt, ta, tb, p, di.sm_count, s);
+  if (pair) return dispatch_bmm_layout<256, true>(a_mn, b_mn, ta, tb, p, di.sm_count, s);
+  if (bn == 256) return dispatch_bmm_layout<256, false>(a_mn, b_mn, ta, tb, p, di.sm_count, s);
+  return dispatch_bmm_layout<128, false>(a_mn, b_mn, ta, tb, p, di.sm_count, s);
 }
 int pcb_bmm_scaled(const void* a, int64_t sab, int64_t sam, int64_t sak, const void* b, int64_t sbb, int64_t sbk,
                    int64_t sbn, int ab_dtype, int64_t batch, int64_t m, int64_t n, int64_t k, const float* scale_a,
@@ -943,7 +999,20 @@ int pcb_bmm_scaled(const void* a, int64_t sab, int64_t sam, int64_t sak, const v
                    int64_t ssbk, int64_t ssbn, int64_t qbn, int64_t qbk, const void* bias, int bias_dtype,
                    int64_t sbib, int64_t sbim, int64_t sbin, void* c, int c_dtype, int64_t scb, int64_t scm,
                    int64_t scn, int activation, void* stream) {
-  return bmm_entry(a, sab, sam, sak, b, sbb, sbk, sbn, ab_dtype, batch, m, n, k, scale_a, ssab, ssam, ssak, qbm, scale_b, ssbb, ssbk, ssbn, qbn, qbk, bias, bias_dtype, sbib, sbim, sbin, c, c_dtype, scb, scm, scn, activation, stream, false);
+  return bmm_entry(a, sab, sam, sak, b, sbb, sbk, sbn, ab_dtype, ab_dtype, batch, m, n, k, scale_a, ssab, ssam, ssak,
+                   qbm, scale_b, ssbb, ssbk, ssbn, qbn, qbk, bias, bias_dtype, sbib, sbim, sbin, c, c_dtype, scb, scm,
+                   scn, activation, stream, false);
+}
+
+int pcb_bmm_scaled_mixed(const void* a, int64_t sab, int64_t sam, int64_t sak, int a_dtype, const void* b,
+                         int64_t sbb, int64_t sbk, int64_t sbn, int b_dtype, int64_t batch, int64_t m, int64_t n,
+                         int64_t k, const float* scale_a, int64_t ssab, int64_t ssam, int64_t ssak, int64_t qbm,
+                         const float* scale_b, int64_t ssbb, int64_t ssbk, int64_t ssbn, int64_t qbn, int64_t qbk,
+                         const void* bias, int bias_dtype, int64_t sbib, int64_t sbim, int64_t sbin, void* c,
+                         int c_dtype, int64_t scb, int64_t scm, int64_t scn, int activation, void* stream) {
+  return bmm_entry(a, sab, sam, sak, b, sbb, sbk, sbn, a_dtype, b_dtype, batch, m, n, k, scale_a, ssab, ssam, ssak,
+                   qbm, scale_b, ssbb, ssbk, ssbn, qbn, qbk, bias, bias_dtype, sbib, sbim, sbin, c, c_dtype, scb, scm,
+                   scn, activation, stream, false);
 }
 
 int pcb_bmm_block_scaled(const void* a, int64_t sab, int64_t sam, int64_t sak, const void* b, int64_t sbb, int64_t sbk,
@@ -953,8 +1022,18 @@ int pcb_bmm_block_scaled(const void* a, int64_t sab, int64_t sam, int64_t sak, c
                          int64_t sbib, int64_t sbim, int64_t sbin, void* c, int c_dtype, int64_t scb, int64_t scm,
                          int64_t scn, int activation, void* workspace,
                          int64_t workspace_bytes, void* stream) {
-  return bmm_entry(a, sab, sam, sak, b, sbb, sbk, sbn, ab_dtype, batch, m, n, k, scale_a, ssab, ssam, ssak, qbm, scale_b, ssbb, ssbk, ssbn, qbn, qbk, bias, bias_dtype, sbib, sbim, sbin, c, c_dtype, scb, scm, scn, activation, stream, true, workspace, workspace_bytes);
+  return bmm_entry(a, sab, sam, sak, b, sbb, sbk, sbn, ab_dtype, ab_dtype, batch, m, n, k, scale_a, ssab, ssam, ssak,
+                   qbm, scale_b, ssbb, ssbk, ssbn, qbn, qbk, bias, bias_dtype, sbib, sbim, sbin, c, c_dtype, scb, scm,
+                   scn, activation, stream, true, workspace, workspace_bytes);
 }
 
+
+#ifdef PCB_GEMM_TRACE
+// Trace builds only: copy CTA 0's cycle stamps (16 x 1024 long long) to host.
+int pcb_trace_read(long long* host) {
+  return cudaMemcpyFromSymbol(host, gemm::g_gemm_trace, sizeof(gemm::g_gemm_trace)) == cudaSuccess ? PCB_OK
+                                                                                                   : PCB_ERR_DEVICE;
+}
+#endif
 
 }  // extern "C"

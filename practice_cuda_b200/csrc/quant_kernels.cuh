@@ -19,17 +19,22 @@ enum ScaleMode : int {
   kDeqReciprocal = 0,  // dequant = 1 / quant_scale     (per-block, per-tensor)
   kDeqDivide = 1,      // dequant = amax / fp8_max       (per-channel)
   kDeqPow2 = 2,        // quant scale a power of two (E8M0), dequant = its reciprocal
+  kQuantDivide = 3,    // dynamic float8 cast: quant scale = fp8_max / amax (one IEEE divide),
+                       // and the stored scale is that quant scale
 };
 
 template <int MODE>
 __device__ __forceinline__ float mode_quant_scale(float safe, float fp8_max) {
   if constexpr (MODE == kDeqPow2) return pow2_quant_scale(safe, fp8_max);
+  else if constexpr (MODE == kQuantDivide) return __fdiv_rn(fp8_max, safe);
   else return quant_scale_from_amax(safe, fp8_max);
 }
 
+// The scale a kernel stores: the dequant scale, or (kQuantDivide) the quant scale.
 template <int MODE>
 __device__ __forceinline__ float mode_dequant_scale(float safe, float fp8_max, float qs) {
   if constexpr (MODE == kDeqDivide) return __fdiv_rn(safe, fp8_max);
+  else if constexpr (MODE == kQuantDivide) return qs;
   else return __frcp_rn(qs);
 }
 
@@ -339,11 +344,8 @@ __global__ void __launch_bounds__(kThreads) quant_groups_generic_kernel(const Ge
     }
     amax = team_max<kThreads>(amax, red);
     const float safe = clamp_min_eps(__uint_as_float(amax), args.eps);
-    const float qs = quant_scale_from_amax(safe, fp8_max);
-    if (threadIdx.x == 0) {
-      const float deq = (MODE == kDeqReciprocal) ? __frcp_rn(qs) : __fdiv_rn(safe, fp8_max);
-      args.scale[b * args.ssb + gi * args.ssm + gj * args.ssn] = deq;
-    }
+    const float qs = mode_quant_scale<MODE>(safe, fp8_max);
+    if (threadIdx.x == 0) args.scale[b * args.ssb + gi * args.ssm + gj * args.ssn] = mode_dequant_scale<MODE>(safe, fp8_max, qs);
     for (int64_t e = threadIdx.x; e < count; e += kThreads) {
       const int64_t r = e / cols, c = e - (e / cols) * cols;
       const float v =
@@ -494,6 +496,9 @@ struct TensorArgs {
   int scale_dtype;
   float fp8_max;
   float eps;
+  // Dynamic float8 cast numerics: quant scale = fp8_max / amax (one fp32
+  // IEEE divide, which equals torchAO's float64 divide rounded to fp32).
+  int quant_divide;
 };
 
 constexpr int kPerTensorMaxPartials = 1024;
@@ -552,7 +557,8 @@ __global__ void __launch_bounds__(kThreads) tensor_cast_kernel(const TensorArgs 
   const float a = __uint_as_float(amax);
   const float eps_dt = round_to(args.eps, dt);
   const float safe = (a < eps_dt) ? eps_dt : a;
-  const float qs = round_to(__fmul_rn(round_to(__frcp_rn(safe), dt), args.fp8_max), dt);
+  const float qs = args.quant_divide ? __fdiv_rn(args.fp8_max, safe)
+                                     : round_to(__fmul_rn(round_to(__frcp_rn(safe), dt), args.fp8_max), dt);
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     if (args.quant_scale) *args.quant_scale = qs;
     if (args.dequant_scale) *args.dequant_scale = round_to(__frcp_rn(qs), dt);

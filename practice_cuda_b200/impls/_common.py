@@ -150,10 +150,21 @@ def bmm_scaled(
         workspace = torch.empty((max(ws_bytes, 16),), dtype=torch.uint8, device=a.device)
         tail = (workspace.data_ptr(), ws_bytes, stream)
 
+    mixed = a.dtype != b.dtype
+    if mixed and block_scaled:
+        raise ValueError(f"block-scaled BMM needs one fp8 format, got A={a.dtype}, B={b.dtype}")
+    if mixed:
+        entry = lib.pcb_bmm_scaled_mixed
+
     def launch(a_t, b_t):
+        if mixed:
+            head = (a_t.data_ptr(), a_t.stride(0), a_t.stride(1), a_t.stride(2), _lib.dtype_code(a_t.dtype),
+                    b_t.data_ptr(), b_t.stride(0), b_t.stride(1), b_t.stride(2), _lib.dtype_code(b_t.dtype))
+        else:
+            head = (a_t.data_ptr(), a_t.stride(0), a_t.stride(1), a_t.stride(2),
+                    b_t.data_ptr(), b_t.stride(0), b_t.stride(1), b_t.stride(2), _lib.dtype_code(a_t.dtype))
         return entry(
-            a_t.data_ptr(), a_t.stride(0), a_t.stride(1), a_t.stride(2),
-            b_t.data_ptr(), b_t.stride(0), b_t.stride(1), b_t.stride(2), _lib.dtype_code(a_t.dtype),
+            *head,
             batch, m, n, k,
             scale_a.data_ptr() if scale_a is not None else None, *sa_strides, qbm,
             scale_b.data_ptr() if scale_b is not None else None, *sb_strides, qbn,
@@ -168,5 +179,5 @@ def bmm_scaled(
     status = launch(a, b)
     if status == _lib.PCB_ERR_LAYOUT and k > 0:
         status = launch(pack_k_major(a, k_dim_last=True), pack_k_major(b, k_dim_last=False))
-    _lib.check(status, "pcb_bmm_block_scaled" if block_scaled else "pcb_bmm_scaled")
+    _lib.check(status, "pcb_bmm_block_scaled" if block_scaled else ("pcb_bmm_scaled_mixed" if mixed else "pcb_bmm_scaled"))
     return out

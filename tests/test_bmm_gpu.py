@@ -237,15 +237,16 @@ def test_zero_k_and_empty():
 
 
 @pytest.mark.parametrize("layout", ["a_k_b_n", "a_k_b_k", "a_m_b_n"])
-def test_per_block_on_cta_pair(layout, monkeypatch):
-    """Per-block scales on the 256x256 CTA-pair kernel (selected by default only
-    for single-K-group tiles; forced here so both kernels stay covered)."""
-    monkeypatch.setenv("PCB200_BMM_PAIR", "2")
-    B, M, K, N = 2, 384, 640, 512
+@pytest.mark.parametrize("m", [128, 384])
+def test_per_block_pair_and_single(layout, m):
+    """Per-block scales on both tile paths: M > 128 runs 256x256 tiles on a
+    CTA pair (M = 384 leaves the second CTA of the last pair idle), M <= 128
+    runs 128x256 tiles on one CTA."""
+    B, M, K, N = 2, m, 640, 512
     a = synthetic((B, M, K), outliers=True, seed=40)
     b = synthetic((B, K, N), std=0.02, seed=41)
     qa, qb, ablk, bblk = _quant_pair("1x128_128x128", a, b)
     ref = _promoted_ref(qa, qb, ablk, bblk)
     qa2, qb2 = _operands_for_layout(qa, qb, layout)
     out = get_bmm(f"b200_per_block_1x128_128x128_{layout}").fn(qa2, qb2)
-    assert_bmm_close(out, ref, f"pair {layout}")
+    assert_bmm_close(out, ref, f"per-block M={m} {layout}")

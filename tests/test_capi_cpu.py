@@ -75,3 +75,17 @@ def test_check_raises_with_status():
     with pytest.raises(_lib.Pcb200Error) as ei:
         _lib.check(_lib.PCB_ERR_LAYOUT, "op")
     assert ei.value.status == _lib.PCB_ERR_LAYOUT
+
+
+def test_new_entry_points_reject_bad_arguments_without_gpu():
+    lib = _lib.lib()
+    # dynamic float8 cast: axiswise must be 0 or 1; fp8 input rejected
+    st = lib.pcb_quant_float8_dynamic(None, 2, 1, 4, 4, 0, 4, 1, None, 3, 0, 4, 1, None, 0, 1, 2, 1e-12, None, None)
+    assert st == _lib.PCB_ERR_INVALID
+    st = lib.pcb_quant_float8_dynamic(1, 3, 1, 4, 4, 0, 4, 1, 1, 3, 0, 4, 1, 1, 0, 1, 1, 1e-12, None, None)
+    assert st == _lib.PCB_ERR_INVALID
+    # mixed-format BMM: B's dtype must be fp8
+    st = lib.pcb_bmm_scaled_mixed(1, 0, 128, 1, 3, 1, 0, 128, 1, 2, 1, 128, 128, 128,
+                                  None, 0, 0, 0, 1, None, 0, 0, 0, 1, 128,
+                                  None, 0, 0, 0, 0, 1, 2, 0, 128, 1, 0, None)
+    assert st == _lib.PCB_ERR_INVALID
