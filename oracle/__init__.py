@@ -8,7 +8,8 @@ path runs the CUDA library and fails loudly when it is missing.
 Parity pin: the restatement is checked against vectors produced by the
 reference's own torch functions (``tests/golden/make_golden.py``) -- the
 per-channel torch quantizer, the legacy per-tensor test reference, and the
-registry's ``QuantResult.dequantize``.
+registry's ``QuantResult.dequantize``, and the FP8 training linear's dynamic
+cast ``hp_tensor_to_float8_dynamic``.
 """
 
 from .quant import (  # noqa: F401
@@ -18,6 +19,7 @@ from .quant import (  # noqa: F401
     per_channel_quant,
     per_tensor_quant,
     legacy_per_tensor_quant,
+    float8_dynamic_cast,
     dequantize,
 )
 from .gemm import (  # noqa: F401

@@ -85,7 +85,8 @@ def per_block_quant_pow2(
     library; the reference has no counterpart): ``r = RN(max(amax, eps) /
     fp8_max)`` in fp32, ``e`` the smallest integer with ``2**e >= r`` (from
     r's exponent and mantissa bits), ``quant_scale = 2**-e``, ``dequant =
-    1 / quant_scale``; a non-finite or subnormal ``r`` gives ``quant_scale =
+    1 / quant_scale``; a zero or subnormal ``r`` is clamped to ``2**-126``
+    (``quant_scale = 2**126``) and a non-finite ``r`` gives ``quant_scale =
     1 / r``.  Tiles, tails and storage as :func:`per_block_quant`.
     """
     if x.ndim not in (2, 3):
@@ -105,7 +106,8 @@ def per_block_quant_pow2(
     ef = (bits >> 23) & 0xFF
     e = ef - 127 + ((bits & 0x7FFFFF) != 0).to(torch.int32)
     pow2 = ((127 - e).clamp(0, 254) << 23).view(torch.float32)
-    quant_scale = torch.where((ef == 0) | (ef == 0xFF), 1.0 / r, pow2)
+    pow2 = torch.where(ef == 0, torch.tensor(2.0 ** 126, dtype=torch.float32), pow2)
+    quant_scale = torch.where(ef == 0xFF, 1.0 / r, pow2)
     dequant_scale = 1.0 / quant_scale
     qs_full = quant_scale.repeat_interleave(block_m, dim=1).repeat_interleave(block_n, dim=2)
     y = torch.clamp(xf * qs_full, min=-fp8_max, max=fp8_max)[:, :m, :n].to(fp8_dtype)
@@ -184,6 +186,32 @@ def legacy_per_tensor_quant(
         x.float() * quant_factor.float(), min=-fp8_range, max=fp8_range
     ).to(quant_dtype)
     return y, reciprocal_factor
+
+
+def float8_dynamic_cast(
+    x: torch.Tensor,
+    fp8_dtype: torch.dtype = torch.float8_e4m3fn,
+    *,
+    axiswise: bool = False,
+    eps: float = 1e-12,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Dynamic float8 cast of the FP8 training linear.
+
+    ``hp_tensor_to_float8_dynamic``
+    (``fp8_training/fp8_bench/modules/float8/float8_scaling_utils.py:29-72``):
+    amax over the whole tensor, or per row over the last dim when
+    ``axiswise`` (``tensor_to_amax``, ``float8_utils.py:56-86``, keepdim);
+    ``scale = f32(fp8_max / clamp(f64(amax), eps))`` (``amax_to_scale``,
+    ``:31-53``); ``data = fp8(clamp(f32(x) * scale, +-fp8_max))``
+    (``to_fp8_saturated`` ``:118-139``, ``float8_training_tensor.py:150-155``).
+    Returns ``(data, scale)``; the scale is the QUANT scale.
+    """
+    xf = x.float()
+    amax = xf.abs().amax(dim=-1, keepdim=True) if axiswise else xf.abs().max()
+    fmax = torch.finfo(fp8_dtype).max
+    scale = (fmax / torch.clamp(amax.to(torch.float64), min=eps)).to(torch.float32)
+    data = torch.clamp(xf * scale, min=-fmax, max=fmax).to(fp8_dtype)
+    return data, scale
 
 
 def dequantize(

@@ -1,4 +1,4 @@
-"""Per-block FP8 training linear (BASELINE cfg5; SURVEY next-step 1).
+"""Per-block FP8 training linear (the FSDP2 FP8 training config).
 
 ``y = x @ w.T`` with all three GEMMs of a training step on the per-block FP8
 path of libpcb200:

@@ -1,4 +1,4 @@
-"""FSDP2 all-gather of per-block FP8 weights (BASELINE cfg5; SURVEY next-step 2).
+"""FSDP2 all-gather of per-block FP8 weights (the FSDP2 FP8 training config).
 
 A linear weight wrapped in :class:`FP8AllGatherWeight` keeps its
 high-precision master values in the FSDP shard, but when FSDP2 unshards it the
@@ -47,12 +47,24 @@ _PRESERVE = {
     torch.ops.aten.alias.default,
 }
 
+# Outputs of these ops alias their input's storage, so the output wrapper
+# shares the input's write generation: a write through either invalidates the
+# cached quantization of both.
+_ALIASING = {
+    torch.ops.aten.slice.Tensor,
+    torch.ops.aten.view.default,
+    torch.ops.aten.as_strided.default,
+    torch.ops.aten.split.Tensor,
+    torch.ops.aten.detach.default,
+    torch.ops.aten.alias.default,
+}
+
 
 class FP8AllGatherWeight(torch.Tensor):
     """High-precision weight whose FSDP2 all-gather is per-block FP8."""
 
     @staticmethod
-    def __new__(cls, tensor: torch.Tensor, pow2: bool = False):
+    def __new__(cls, tensor: torch.Tensor, pow2: bool = False, gen: Optional[list] = None):
         return torch.Tensor._make_wrapper_subclass(
             cls,
             tensor.size(),
@@ -64,9 +76,15 @@ class FP8AllGatherWeight(torch.Tensor):
             requires_grad=tensor.requires_grad,
         )
 
-    def __init__(self, tensor: torch.Tensor, pow2: bool = False):
+    def __init__(self, tensor: torch.Tensor, pow2: bool = False, gen: Optional[list] = None):
         self._tensor = tensor
         self._pow2 = pow2  # power-of-two (E8M0) scales for the block-scaled GEMM
+        # Write generation, one cell shared by every wrapper that aliases the
+        # same storage (views, .data, .detach()).  The autograd-level version
+        # counter does not see writes made through a .data alias (it gets a
+        # fresh counter) nor those made below the Python dispatch key, so the
+        # cache is keyed on this cell instead.
+        self._gen = gen if gen is not None else [0]
 
     def __repr__(self):
         return f"FP8AllGatherWeight({self._tensor!r})"
@@ -81,26 +99,33 @@ class FP8AllGatherWeight(torch.Tensor):
     @classmethod
     def __torch_dispatch__(cls, func, types, args=(), kwargs=None):
         kwargs = kwargs or {}
+        wrapped = [t for t in tree_flatten((args, kwargs))[0] if isinstance(t, FP8AllGatherWeight)]
         if func._schema.is_mutable:
             # Any op that may write a weight (optimizer updates, FSDP's
-            # copy-in) invalidates its cached quantization.
-            for t in tree_flatten((args, kwargs))[0]:
-                if isinstance(t, FP8AllGatherWeight):
-                    t._mutations = getattr(t, "_mutations", 0) + 1
-        pow2 = any(t._pow2 for t in tree_flatten((args, kwargs))[0] if isinstance(t, FP8AllGatherWeight))
+            # copy-in, writes through an alias) invalidates its cached
+            # quantization and that of every wrapper aliasing it.
+            for t in wrapped:
+                t._gen[0] += 1
+        pow2 = any(t._pow2 for t in wrapped)
+        gen = wrapped[0]._gen if (func in _ALIASING and wrapped) else None
         args, kwargs = tree_map_only(FP8AllGatherWeight, lambda t: t._tensor, (args, kwargs))
         out = func(*args, **kwargs)
         if func not in _PRESERVE:
             return out
-        return tree_map_only(torch.Tensor, lambda t: FP8AllGatherWeight(t, pow2), out)
+        return tree_map_only(torch.Tensor, lambda t: FP8AllGatherWeight(t, pow2, gen), out)
 
     # ---- FSDP2 all-gather extension -------------------------------------------
     def _quantized_shard(self, world: int):
-        """All-gather inputs for the current shard values, cached until an
-        op that may write the weight runs on it (counted in
-        ``__torch_dispatch__``), so the backward re-gather and
-        :func:`precompute_fp8_block_weights` do not quantize twice."""
-        key = (getattr(self, "_mutations", 0), world)
+        """All-gather inputs for the current shard values, cached until the
+        shard may have been written, so the backward re-gather and
+        :func:`precompute_fp8_block_weights` do not quantize twice.
+
+        The key is the write generation shared by all wrappers of this
+        storage (bumped by every mutable op dispatched on any of them,
+        including ``w.data.add_`` and ``w.detach().copy_``), the inner
+        tensor's own version counter and its storage pointer (FSDP may swap
+        the storage)."""
+        key = (self._gen[0], self._tensor._version, self._tensor.data_ptr(), world)
         cached = getattr(self, "_fp8_cache", None)
         if cached is not None and cached[0] == key:
             return self._fresh(cached[1], world), cached[2]

@@ -202,3 +202,53 @@ def get_bmm(name: str) -> BMMImpl:
         return BMM_IMPLS[name]
     except KeyError as exc:
         raise KeyError(f"unknown BMM implementation {name}; choices={sorted(BMM_IMPLS)}") from exc
+
+
+def install_into(ref_registry, prefix: str = "b200_") -> list[str]:
+    """Register this library's implementations (names starting with
+    ``prefix``) in another registry module with this contract -- normally
+    the reference's own ``fp8_bench.registry`` -- so its harnesses
+    (``bench_quant``, ``bench_bmm``, ``profile_one``, ``report``) list and run
+    them next to the built-in Triton impls.  Quant functions are wrapped to
+    return that module's ``QuantResult`` class; BMM functions read operands
+    by attribute and accept either class.  The target's built-ins are loaded
+    first (``load_builtin_impls``) so they cannot collide later.  Returns the
+    names installed (already-present names are skipped)."""
+    load_builtin_impls()
+    ref_registry.load_builtin_impls()
+    ref_qr = ref_registry.QuantResult
+
+    def wrap_quant(fn):
+        def quant(*args, **kwargs):
+            r = fn(*args, **kwargs)
+            return ref_qr(r.tensor, r.dequant_scale, r.impl, r.granularity, dict(r.meta))
+
+        quant.__wrapped__ = fn
+        return quant
+
+    def wrap_prepare(fn):
+        def prepare(value):
+            out = fn(value)
+            if isinstance(out, QuantResult):
+                return ref_qr(out.tensor, out.dequant_scale, out.impl, out.granularity, dict(out.meta))
+            return out
+
+        return prepare
+
+    installed = []
+    order = getattr(ref_registry, "_BMM_QUANT_ORDER", None)
+    for name, q in QUANT_IMPLS.items():
+        if name.startswith(prefix) and name not in ref_registry.QUANT_IMPLS:
+            ref_registry.register_quant(name, wrap_quant(q.fn), q.description, get_best_config=q.get_best_config)
+            if order is not None:
+                order.setdefault(name, len(order))
+            installed.append(name)
+    for name, b in BMM_IMPLS.items():
+        if name.startswith(prefix) and name not in ref_registry.BMM_IMPLS:
+            ref_registry.register_bmm(
+                name, b.fn, quant_impl=b.quant_impl, layout=b.layout, prepare_b=wrap_prepare(b.prepare_b),
+                a_layout=b.a_layout, prepare_a=wrap_prepare(b.prepare_a), quant_a_kwargs=b.quant_a_kwargs,
+                quant_b_kwargs=b.quant_b_kwargs, prepare_call_kwargs=b.prepare_call_kwargs,
+                description=b.description, get_best_config=b.get_best_config)
+            installed.append(name)
+    return installed

@@ -13,6 +13,9 @@ produced by a function of the reference itself, evaluated eagerly on the CPU:
   ``q = max / amax``, ``deq = q.reciprocal()``) -- so each tile's bytes and
   scale are produced by calling ``fp8_quant_ref`` on that tile (fp32);
 * per-tensor quant: ``fp8_quant_ref`` (E4M3 and E5M2);
+* dynamic float8 casts of the FP8 training linear: ``hp_tensor_to_float8_dynamic``
+  (``fp8_training/fp8_bench/modules/float8/float8_scaling_utils.py:29-72``),
+  tensorwise and axiswise (``axiswise_dim=-1``), E4M3 and E5M2;
 * scaled BMM: the registry's ``QuantResult.dequantize`` followed by an fp32
   ``torch.bmm`` (``bench_bmm.py:414-419``), and the legacy ``fp8_quant_bmm_ref``
   (``kernels/fp8_bmm/test/fp8_quant_bmm_test.py:100-114``).
@@ -135,6 +138,26 @@ def main() -> None:
         y, r = fp8_quant_ref(x, quant_dtype=dt, fp8_range=rng)
         cases[name] = {"kind": "per_tensor", "x": x, "fp8_dtype": str(dt), "fp8_range": rng,
                        "y_u8": u8(y), "scale": r.clone()}
+
+    # ---- dynamic float8 casts (FP8 training linear) ---------------------------
+    from fp8_bench.modules.float8.config import ScalingGranularity
+    from fp8_bench.modules.float8.float8_scaling_utils import hp_tensor_to_float8_dynamic
+    from fp8_bench.modules.float8.float8_training_tensor import LinearMMConfig
+
+    zero_row = synthetic((2, 6, 96), seed=27)
+    zero_row[1, 3].zero_()
+    for name, x in [
+        ("f8dyn_bf16", synthetic((2, 40, 264), outliers=True, seed=28)),
+        ("f8dyn_f32", synthetic((3, 17, 48), std=0.02, seed=29, dtype=torch.float32)),
+        ("f8dyn_bf16_zero_row", zero_row),
+    ]:
+        for dt in (e4m3, torch.float8_e5m2):
+            for axis in (False, True):
+                kw = ({"scaling_granularity": ScalingGranularity.AXISWISE, "axiswise_dim": -1} if axis else {})
+                t = hp_tensor_to_float8_dynamic(x, dt, LinearMMConfig(), **kw)
+                cases[f"{name}_{str(dt).split('_')[-1]}_{'axis' if axis else 'tensor'}"] = {
+                    "kind": "float8_dynamic", "x": x, "fp8_dtype": str(dt), "axiswise": axis,
+                    "y_u8": u8(t._data), "scale": t._scale.clone()}
 
     # ---- scaled BMM: registry dequantize + fp32 bmm --------------------------
     def bmm_case(name, a_x, b_x, a_kind, b_kind, bias=None):

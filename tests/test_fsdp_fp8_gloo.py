@@ -86,6 +86,18 @@ def _worker(rank, world, port, q):
         ok = ok and ff.precompute_fp8_block_weights(m) == 1 and len(calls) == 3
         m(torch.randn(2, 384))
         ok = ok and matches(w2) and len(calls) == 3
+        # Writes through aliases of the parameter (what EMA updates and
+        # checkpoint loaders do via .data / .detach()) also invalidate it.
+        for alias in (lambda w: w.data, lambda w: w.detach()):
+            m.reshard()
+            with torch.no_grad():
+                local = m[0].weight
+                local = getattr(local, "_local_tensor", local)
+                alias(local).add_(alias(local) * 0 + 0.001)
+            w3 = m[0].weight.full_tensor()
+            before = len(calls)
+            m(torch.randn(2, 384))
+            ok = ok and matches(w3) and len(calls) == before + 1
         q.put((rank, bool(ok)))
     finally:
         dist.destroy_process_group()

@@ -19,7 +19,7 @@ def _cases(golden, kind):
 
 def test_golden_has_all_kinds(golden):
     kinds = {v["kind"] for v in golden.values()}
-    assert kinds == {"per_channel", "per_block", "per_tensor", "bmm", "legacy_bmm"}
+    assert kinds == {"per_channel", "per_block", "per_tensor", "bmm", "legacy_bmm", "float8_dynamic"}
 
 
 def test_per_channel(golden):
@@ -49,6 +49,19 @@ def test_per_tensor_legacy(golden):
             y2, r2 = oracle.per_tensor_quant(c["x"])
             assert torch.equal(_u8(y2), c["y_u8"]), name
             assert torch.equal(r2, c["scale"]), name
+
+
+def test_float8_dynamic_cast(golden):
+    """The FP8 training linear's dynamic casts (tensorwise / axiswise, E4M3 /
+    E5M2) against the reference's hp_tensor_to_float8_dynamic."""
+    names = _cases(golden, "float8_dynamic")
+    assert len(names) == 12
+    for name in names:
+        c = golden[name]
+        dt = torch.float8_e5m2 if "e5m2" in c["fp8_dtype"] else E4M3
+        y, s = oracle.float8_dynamic_cast(c["x"], dt, axiswise=c["axiswise"])
+        assert torch.equal(_u8(y), c["y_u8"]), name
+        assert s.shape == c["scale"].shape and torch.equal(s, c["scale"]), name
 
 
 def _gran(kind):
