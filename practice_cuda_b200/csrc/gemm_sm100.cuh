@@ -35,11 +35,18 @@ constexpr int kEpiThreads = 256;
 // accumulators per thread.  The launch holds kThreads * kLaunchRegs registers
 // (checked on the host before every launch) and the split adds up to it.
 constexpr int kLaunchRegs = 168;  // 65536 / 384, rounded down to a multiple of 8
+#ifdef PCB_GEMM_LOW_REGS
+constexpr int kLowRegs = PCB_GEMM_LOW_REGS;
+constexpr int kHighRegs = (kThreads * kLaunchRegs - 128 * kLowRegs) / 256;
+#else
 constexpr int kLowRegs = 40;
 constexpr int kHighRegs = 232;
+#endif
 static_assert(128 * kLowRegs + 256 * kHighRegs == kThreads * kLaunchRegs, "register split must match the launch");
+#ifndef PCB_GEMM_EPI_CW
+#define PCB_GEMM_EPI_CW 64  // TMEM columns per epilogue load (16, 32 or 64)
+#endif
 constexpr int kNumAcc = 4;        // TMEM accumulator buffers of BN fp32 columns
-constexpr int kScalePrefetch = 4;  // K groups of scales kept in flight per epilogue thread
 
 // Profiling switches (Params::debug_flags) exist only in builds compiled with
 // -DPCB200_PROFILING; the shipped library compiles every check below to false.
@@ -235,6 +242,25 @@ __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[3
       : "r"(taddr));
 }
 
+// 64 consecutive fp32 columns of this thread's TMEM lane (no wait).
+__device__ __forceinline__ void tmem_ld64_nowait(uint32_t taddr, uint32_t (&r)[64]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
+      "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+        "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+        "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+        "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+        "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr));
+}
+
 // 16 consecutive fp32 columns of this thread's TMEM lane (no wait).
 __device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
@@ -243,6 +269,14 @@ __device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[1
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
+}
+
+// N (16, 32 or 64) consecutive fp32 columns of this thread's TMEM lane (no wait).
+template <int N>
+__device__ __forceinline__ void tmem_ld_n(uint32_t taddr, uint32_t (&r)[N]) {
+  if constexpr (N == 64) tmem_ld64_nowait(taddr, r);
+  else if constexpr (N == 32) tmem_ld32_nowait(taddr, r);
+  else tmem_ld16_nowait(taddr, r);
 }
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
@@ -640,8 +674,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int i = 0; i < EPI_COLS / 2; ++i) acc[i] = make_float2(0.f, 0.f);
 
-      // Scales of the next kScalePrefetch groups stay in flight in registers
-      // (the group loop is unrolled by kScalePrefetch so the ring indices are static).
       auto row_scale = [&](int g) -> float {
         return (sa_row && row_ok) ? __ldg(sa_row + (long long)g * p.ssak) : 1.f;
       };
@@ -663,24 +695,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       };
       if constexpr (!COL_UNIFORM) load_cols(0);
-      float rs[kScalePrefetch], cs[kScalePrefetch];
-#pragma unroll
-      for (int j = 0; j < kScalePrefetch; ++j) {
-        rs[j] = (j < p.num_groups) ? row_scale(j) : 1.f;
-        cs[j] = (j < p.num_groups) ? col_scale(j) : 1.f;
-      }
-      for (int g0 = 0; g0 < p.num_groups && ok; g0 += kScalePrefetch) {
-#pragma unroll
-        for (int j = 0; j < kScalePrefetch; ++j) {
-          const int g = g0 + j;
-          if (g >= p.num_groups || !ok) break;
+      // The scales of the next two K groups are in flight in registers
+      // (shifted down each group).  The group loop is not unrolled: its
+      // body already holds the 128 accumulators and a 64-column TMEM load.
+      float rs0 = row_scale(0), cs0 = col_scale(0);
+      float rs1 = (1 < p.num_groups) ? row_scale(1) : 1.f, cs1 = (1 < p.num_groups) ? col_scale(1) : 1.f;
+#pragma unroll 1
+      for (int g = 0; g < p.num_groups && ok; ++g) {
+        {
           const uint32_t abuf = acc_cnt % NACC;
           const uint32_t aphase = (acc_cnt / NACC) & 1;
-          const float s_row = rs[j];
-          const float s_col = cs[j];
-          if (g + kScalePrefetch < p.num_groups) {
-            rs[j] = row_scale(g + kScalePrefetch);
-            cs[j] = col_scale(g + kScalePrefetch);
+          const float s_row = rs0;
+          const float s_col = cs0;
+          rs0 = rs1;
+          cs0 = cs1;
+          if (g + 2 < p.num_groups) {
+            rs1 = row_scale(g + 2);
+            cs1 = col_scale(g + 2);
           }
           if constexpr (!COL_UNIFORM) {
             // Publish this group's column scales (loaded one group ahead) to
@@ -736,20 +767,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                                              s2, acc[c * 16 + i]);
               }
           } else {
-            // Wide half-tile: 16-column chunks; the TMEM load of chunk c+1 is
-            // in flight while chunk c is promoted, and the buffer is released
-            // as soon as the last chunk has landed in registers.
-            constexpr int CW = 16;
+            // Wide half-tile: CW-column TMEM loads, one round trip each
+            // (the TMEM load latency, not the FMAs, bounds this loop); the
+            // buffer is released as soon as the last load has landed.
+            constexpr int CW = PCB_GEMM_EPI_CW;
             constexpr int NCH = EPI_COLS / CW;
-            uint32_t v[2][CW];
-            tmem_ld16_nowait(taddr, v[0]);
 #pragma unroll
             for (int c = 0; c < NCH; ++c) {
+              uint32_t vc[CW];
+              tmem_ld_n(taddr + c * CW, vc);
               tmem_wait_ld();
-              tmem_regs_ready(v[c & 1]);
-              if (c + 1 < NCH) {
-                tmem_ld16_nowait(taddr + (c + 1) * CW, v[(c + 1) & 1]);
-              } else {
+              tmem_regs_ready(vc);
+              if (c + 1 == NCH) {
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
@@ -758,7 +787,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (threadIdx.x == 128) PCB_TRACE(6, acc_cnt);
               }
-              const uint32_t* vc = v[c & 1];
               if constexpr (COL_UNIFORM) {
                 const float2 s2 = make_float2(s_row * s_col, s_row * s_col);
 #pragma unroll

@@ -100,14 +100,25 @@ struct Chunk {
       }
     }
   }
+  // Elements 2j, 2j+1 as fp32 (16-bit inputs).
+  __device__ __forceinline__ float2 pair(int j) const {
+    const uint32_t w = word(j);
+    if constexpr (XT == PCB_DTYPE_BF16) {
+      return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+    } else {
+      return __half22float2(*reinterpret_cast<const __half2*>(&w));
+    }
+  }
   template <int YT>
   __device__ __forceinline__ void store(uint8_t* q, float qs) const {
     if constexpr (VEC == 8) {
+      // Two IEEE fp32 products per FMUL2 (bit-identical to two __fmul_rn).
+      const float2 q2 = make_float2(qs, qs);
+      const float2 p0 = __fmul2_rn(pair(0), q2), p1 = __fmul2_rn(pair(1), q2);
+      const float2 p2 = __fmul2_rn(pair(2), q2), p3 = __fmul2_rn(pair(3), q2);
       uint2 out;
-      out.x = (uint32_t)cvt2_fp8<YT>(__fmul_rn(v(0), qs), __fmul_rn(v(1), qs)) |
-              ((uint32_t)cvt2_fp8<YT>(__fmul_rn(v(2), qs), __fmul_rn(v(3), qs)) << 16);
-      out.y = (uint32_t)cvt2_fp8<YT>(__fmul_rn(v(4), qs), __fmul_rn(v(5), qs)) |
-              ((uint32_t)cvt2_fp8<YT>(__fmul_rn(v(6), qs), __fmul_rn(v(7), qs)) << 16);
+      out.x = (uint32_t)cvt2_fp8<YT>(p0.x, p0.y) | ((uint32_t)cvt2_fp8<YT>(p1.x, p1.y) << 16);
+      out.y = (uint32_t)cvt2_fp8<YT>(p2.x, p2.y) | ((uint32_t)cvt2_fp8<YT>(p3.x, p3.y) << 16);
       *reinterpret_cast<uint2*>(q) = out;
     } else {
       uint32_t out = (uint32_t)cvt2_fp8<YT>(__fmul_rn(v(0), qs), __fmul_rn(v(1), qs)) |
