@@ -112,6 +112,25 @@ __device__ __forceinline__ bool mbar_spin_bounded(uint32_t bar, uint32_t parity,
   return false;
 }
 
+// Warp-collective form of mbar_spin_bounded: every lane of the warp polls and
+// the loop exits on a vote, so the result and the control flow stay uniform
+// across the warp.
+__device__ __forceinline__ bool mbar_spin_bounded_warp(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                                       int site) {
+  if (__all_sync(0xffffffffu, mbar_test_wait(bar, parity))) return true;
+  const unsigned long long t0 = global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (__all_sync(0xffffffffu, mbar_test_wait(bar, parity))) return true;
+    if ((i & 255u) == 0u) {
+      if (__any_sync(0xffffffffu, *abort_flag != 0)) return false;
+      if (__any_sync(0xffffffffu, global_timer_ns() - t0 > kWaitLimitNs)) break;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) report_error(PCB_ERR_TIMEOUT, site);
+  *abort_flag = 1;
+  return false;
+}
+
 // Bounded wait on phase `parity` of an mbarrier.  Returns false (after
 // recording an error and raising the CTA abort flag) when the wait runs out
 // or when another warp of the CTA already aborted.

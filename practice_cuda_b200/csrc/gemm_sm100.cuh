@@ -4,8 +4,10 @@
 //
 // CTA = 12 warps, persistent over output tiles (one CTA per SM):
 //   warp 0      TMA producer (one elected lane), no multicast
-//   warp 1      TMEM allocator + MMA issuer (one elected lane)
-//   warps 2-3   idle (they only give their registers to the epilogue)
+//   warp 1      TMEM allocator + MMA issuer (warp-uniform loop, elect.sync
+//               lane issues)
+//   warps 2-3   scale loader: each tile's fp32 scales, W K groups at a time,
+//               into a two-slot shared ring read by the epilogue
 //   warps 4-11  epilogue: two warpgroups; warpgroup h owns tile columns
 //               [h*BN/2, (h+1)*BN/2), warp (w % 4) owns TMEM lanes / rows
 //               [32*(w%4), 32*(w%4)+32).
@@ -18,6 +20,8 @@
 // read their own TMEM half and arrive on the leader's accumulator-empty
 // barrier (plain remote arrives, no cluster-scope release).
 #pragma once
+
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -39,14 +43,16 @@ constexpr int kLaunchRegs = 168;  // 65536 / 384, rounded down to a multiple of 
 constexpr int kLowRegs = PCB_GEMM_LOW_REGS;
 constexpr int kHighRegs = (kThreads * kLaunchRegs - 128 * kLowRegs) / 256;
 #else
-constexpr int kLowRegs = 40;
-constexpr int kHighRegs = 232;
+constexpr int kLowRegs = 56;   // producer, MMA issuer, scale loader
+constexpr int kHighRegs = 224;
 #endif
 static_assert(128 * kLowRegs + 256 * kHighRegs == kThreads * kLaunchRegs, "register split must match the launch");
 #ifndef PCB_GEMM_EPI_CW
 #define PCB_GEMM_EPI_CW 64  // TMEM columns per epilogue load (16, 32 or 64)
 #endif
 constexpr int kNumAcc = 4;        // TMEM accumulator buffers of BN fp32 columns
+constexpr int kScaleWin = 8;      // K groups of scales per shared-memory window
+constexpr int kScaleThreads = 64; // scale-loader threads (warps 2-3)
 
 // Profiling switches (Params::debug_flags) exist only in builds compiled with
 // -DPCB200_PROFILING; the shipped library compiles every check below to false.
@@ -64,9 +70,17 @@ __device__ long long g_gemm_trace[16][1024];
   do {                                                                       \
     if (blockIdx.x == 0 && (idx) < 1024) g_gemm_trace[ev][idx] = clock64(); \
   } while (0)
+__device__ unsigned long long g_cta_span[2][1024];  // per-CTA start / end (globaltimer ns)
+#define PCB_CTA_SPAN(i) \
+  do {                  \
+    if (threadIdx.x == 0 && blockIdx.x < 1024) g_cta_span[i][blockIdx.x] = global_timer_ns(); \
+  } while (0)
 #else
 #define PCB_TRACE(ev, idx) \
   do {                     \
+  } while (0)
+#define PCB_CTA_SPAN(i) \
+  do {                  \
   } while (0)
 #endif
 
@@ -105,8 +119,8 @@ struct Params {
   // Block-scaled GEMM only: packed E8M0 scale factors (pack_sf_kernel layout).
   const uint4* sfa;
   const uint4* sfb;
-  int debug_flags;  // PCB200_PROFILING builds only: 1 = epilogue skips its math, 2 = no MMAs issued, 4 = MMA ignores tmem-empty,
-                   // 8 = fused quantizer skipped, 16 = no spin waits on a pair, 32 = spin waits on one CTA
+  int debug_flags;  // PCB200_PROFILING builds only: 1 = epilogue skips its math, 2 = no MMAs issued,
+                   // 8 = fused quantizer skipped
 };
 
 // ---------------------------------------------------------------------------
@@ -209,25 +223,57 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
   asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
-// M=256 MMA over the CTA pair: A rows and B columns split between the two
-// CTAs' shared memory at the same offsets; issued by the leader only.
-__device__ __forceinline__ void umma_f8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                             uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
+
+// Warp-uniform forms: every lane of the warp executes them and the lane
+// chosen by elect.sync issues the instruction, so the issuing loop runs as
+// convergent warp code instead of a one-lane divergent branch.  Descriptors
+// are passed as their low and high 32-bit words (only the low word, start
+// address and LBO, changes from stage to stage).  PAIR selects cta_group::2
+// (M = 256 over the CTA pair, commits multicast to both CTAs).
+template <bool PAIR>
+__device__ __forceinline__ void umma_f8_elect(uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi, uint32_t b_lo,
+                                              uint32_t b_hi, uint32_t idesc, uint32_t accumulate) {
+  if constexpr (PAIR) {
+    asm volatile(
+        "{\n\t.reg .pred e, p;\n\t.reg .b64 ad, bd;\n\t"
+        "mov.b64 ad, {%1, %2};\n\t"
+        "mov.b64 bd, {%3, %4};\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "setp.ne.b32 p, %6, 0;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], ad, bd, %5, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred e, p;\n\t.reg .b64 ad, bd;\n\t"
+        "mov.b64 ad, {%1, %2};\n\t"
+        "mov.b64 bd, {%3, %4};\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "setp.ne.b32 p, %6, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], ad, bd, %5, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
+        : "memory");
+  }
 }
 
-// Arrive on `bar` in both CTAs of the pair once the leader's MMAs retire.
-__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
-      "h"((uint16_t)0x3)
-      : "memory");
+template <bool PAIR>
+__device__ __forceinline__ void umma_commit_elect(uint32_t bar) {
+  if constexpr (PAIR) {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n\t}" ::"r"(bar),
+        "h"((uint16_t)0x3)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(bar)
+        : "memory");
+  }
 }
+
 
 // 32 consecutive fp32 columns of this thread's TMEM lane (no wait).
 __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
@@ -314,23 +360,18 @@ template <int BN, bool PAIR = false>
 struct Smem {
   // A CTA pair splits the B tile: each CTA stages BN/2 of its N rows.
   static constexpr int B_ROWS = PAIR ? BN / 2 : BN;
-#ifdef PCB_GEMM_PAIR_STAGES
-  static constexpr int STAGES = (BN == 256 && !PAIR) ? 4 : PCB_GEMM_PAIR_STAGES;
-#else
   static constexpr int STAGES = (BN == 256 && !PAIR) ? 4 : 6;
-#endif
   static constexpr int A_BYTES = BM * BK;      // 16 KB
   static constexpr int B_BYTES = B_ROWS * BK;  // 32 / 16 KB
   static constexpr int EPI_COLS = BN / 2;
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
   static constexpr int OFF_COLSCALE = OFF_B + STAGES * B_BYTES;           // 8 warps x EPI_COLS floats
-#ifdef PCB_GEMM_NO_COLSCALE
-  static constexpr int OFF_BAR = OFF_COLSCALE;
-#else
-  static constexpr int OFF_BAR = OFF_COLSCALE + 8 * EPI_COLS * 4;
-#endif
-  static constexpr int NUM_BARS = 2 * STAGES + 2 * kNumAcc;
+  // Scale ring slot: row scales [kScaleWin][BM], then uniform B scales [kScaleWin][2].
+  static constexpr int SC_SLOT = kScaleWin * (BM + 2);
+  static constexpr int OFF_SCALE = OFF_COLSCALE + 8 * EPI_COLS * 4;
+  static constexpr int OFF_BAR = OFF_SCALE + 2 * SC_SLOT * 4;
+  static constexpr int NUM_BARS = 2 * STAGES + 2 * kNumAcc + 4;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;                  // tmem addr, abort flag
   static constexpr int BYTES = OFF_MISC + 16;
   static constexpr int ALLOC = BYTES + 1024;                              // slack for 1 KB alignment
@@ -426,9 +467,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   using S = Smem<BN, PAIR>;
   constexpr int STAGES = S::STAGES;
   constexpr int EPI_COLS = S::EPI_COLS;
-  constexpr int NACC = (BN == 256) ? 2 : kNumAcc;
+  constexpr int NACC = (BN == 256) ? 2 : kNumAcc;  // TMEM accumulator buffers of BN columns
   constexpr uint32_t TMEM_COLS = NACC * BN;
   static_assert(NACC * BN <= 512, "TMEM holds 512 fp32 columns");
+  constexpr int W = kScaleWin;
   const uint32_t IDESC = make_idesc(BN, p.a_fmt, p.b_fmt, A_MN ? 1 : 0, B_MN ? 1 : 0, PAIR ? 2 * BM : BM);
   // Bytes that land on the (leader's) full barrier per stage.
   constexpr uint32_t STAGE_TX = (PAIR ? 2 : 1) * (S::A_BYTES + S::B_BYTES);
@@ -441,6 +483,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t bar_empty = bar_full + 8 * STAGES;               // [STAGES]
   const uint32_t bar_tfull = bar_empty + 8 * STAGES;              // [NACC]
   const uint32_t bar_tempty = bar_tfull + 8 * kNumAcc;            // [NACC]
+  const uint32_t bar_sfull = bar_tempty + 8 * kNumAcc;            // [2] scale window loaded
+  const uint32_t bar_sempty = bar_sfull + 16;                     // [2] scale window consumed
+  float* sring = reinterpret_cast<float*>(smem + S::OFF_SCALE);   // [2][S::SC_SLOT]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 4);
 
@@ -451,13 +496,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
   const bool leader = rank == 0;
   const int first_tile = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
-  // Waits whose arrival may come from the peer CTA poll without suspending
-  // (flag 16 switches back to the suspending try_wait, profiling only).
-  const bool spin = (PAIR && !(kProfiling && (p.debug_flags & 16))) || (kProfiling && (p.debug_flags & 32));
-  auto wait = [&](uint32_t bar, uint32_t parity, int site) -> bool {
-    return spin ? mbar_spin_bounded(bar, parity, abort_flag, site) : mbar_wait_bounded(bar, parity, abort_flag, site);
-  };
   const int tile_step = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  // Waits whose arrival may come from the peer CTA poll without suspending.
+  auto wait = [&](uint32_t bar, uint32_t parity, int site) -> bool {
+    return PAIR ? mbar_spin_bounded(bar, parity, abort_flag, site) : mbar_wait_bounded(bar, parity, abort_flag, site);
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -467,6 +510,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < NACC; ++i) {
       mbar_init(bar_tfull + 8 * i, 1);
       mbar_init(bar_tempty + 8 * i, PAIR ? 16 : 8);  // one arrive per epilogue warp (of both CTAs)
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar_sfull + 8 * i, kScaleThreads);  // every scale-loader thread
+      mbar_init(bar_sempty + 8 * i, 8);             // every epilogue warp of this CTA
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -484,7 +531,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-
+  PCB_CTA_SPAN(0);
 
   if (p.inject_error && blockIdx.x == 0 && threadIdx.x == 0) report_error(p.inject_error, SITE_GEMM_INJECTED);
 
@@ -498,38 +545,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      // L2 prefetch cursor: the (tile, k stage) `pf_dist` stages ahead of the loads.
-      const int pf_dist = (kProfiling && (p.debug_flags & 64)) ? ((p.debug_flags >> 8) & 255) : 0;
-      int pf_tile = first_tile, pf_ks = 0;
       int pcnt = 0;  // stages issued (trace index)
       (void)pcnt;
-      auto pf_advance = [&]() {
-        if (++pf_ks == p.k_stages) {
-          pf_ks = 0;
-          pf_tile += tile_step;
-        }
-      };
-      auto pf_issue = [&]() {
-        if (pf_tile >= p.num_tiles) return;
-        const int pb = pf_tile / tiles_per_batch;
-        const int prem = pf_tile - pb * tiles_per_batch;
-        const int pmb = prem / p.n_blocks;
-        const int pnb = prem - pmb * p.n_blocks;
-        const int pa_row = pmb * TILE_M + (int)rank * BM;
-        const int pb_col = pnb * BN + (int)rank * S::B_ROWS;
-        if constexpr (A_MN) tma_prefetch_3d(&tmap_a, pa_row, pf_ks * BK, pb);
-        else tma_prefetch_3d(&tmap_a, pf_ks * BK, pa_row, pb);
-        if constexpr (B_MN) {
-#pragma unroll
-          for (int j = 0; j < S::B_ROWS / 128; ++j) tma_prefetch_3d(&tmap_b, pb_col + j * 128, pf_ks * BK, pb);
-        } else {
-          tma_prefetch_3d(&tmap_b, pf_ks * BK, pb_col, pb);
-        }
-      };
-      for (int i = 0; i < pf_dist; ++i) {
-        pf_issue();
-        pf_advance();
-      }
       for (int tile = first_tile; tile < p.num_tiles && ok; tile += tile_step) {
         const int b = tile / tiles_per_batch;
         const int rem = tile - b * tiles_per_batch;
@@ -538,10 +555,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int a_row = mb * TILE_M + (int)rank * BM;           // this CTA's A rows
         const int b_col = nb * BN + (int)rank * S::B_ROWS;        // this CTA's B columns
         for (int ks = 0; ks < p.k_stages; ++ks) {
-          if (pf_dist) {
-            pf_issue();
-            pf_advance();
-          }
           PCB_TRACE(8, pcnt);
           if (!wait(bar_empty + 8 * stage, phase ^ 1, SITE_GEMM_PRODUCER)) {
             ok = false;
@@ -587,62 +600,150 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------- MMA issuer -------------------------------
-    if (lane == 0 && leader) {
+    // Warp-uniform issuer: all lanes run the loop and poll the barriers with
+    // collective bounded waits; the elect.sync lane issues the MMAs and
+    // commits (a one-lane divergent loop costs hundreds of cycles per group).
+    if (leader) {
       int stage = 0;
       uint32_t phase = 0;
-      uint32_t acc_cnt = 0;
       bool ok = true;
-      for (int tile = first_tile; tile < p.num_tiles && ok; tile += tile_step) {
-        for (int g = 0; g < p.num_groups && ok; ++g) {
-          const uint32_t abuf = acc_cnt % NACC;
-          const uint32_t aphase = (acc_cnt / NACC) & 1;
-          PCB_TRACE(0, acc_cnt);
-          if (!(kProfiling && (p.debug_flags & 4)) && !wait(bar_tempty + 8 * abuf, aphase ^ 1, SITE_GEMM_MMA)) {
+      const uint64_t ad64 = make_sw128_desc(s_base + S::OFF_A, A_MN ? (uint32_t)(128 * BK) : 16u);
+      const uint64_t bd64 = make_sw128_desc(s_base + S::OFF_B, B_MN ? (uint32_t)(128 * BK) : 16u);
+      const uint32_t a_lo0 = (uint32_t)ad64, a_hi = (uint32_t)(ad64 >> 32);
+      const uint32_t b_lo0 = (uint32_t)bd64, b_hi = (uint32_t)(bd64 >> 32);
+      auto uwait = [&](uint32_t bar, uint32_t parity) -> bool {
+        return mbar_spin_bounded_warp(bar, parity, abort_flag, SITE_GEMM_MMA);
+      };
+      // The four MMAs of the smem stage in `stage` into accumulator `d_tmem`
+      // (the first of them overwrites it when `fresh`).
+      auto issue_stage = [&](uint32_t d_tmem, bool fresh) {
+        tc_fence_after();
+        // Stage offsets go into the descriptors' start-address field (addr >> 4).
+        const uint32_t a_lo = a_lo0 + (uint32_t)((stage * S::A_BYTES) >> 4);
+        const uint32_t b_lo = b_lo0 + (uint32_t)((stage * S::B_BYTES) >> 4);
+#pragma unroll
+        for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+          // K advance: 32 bytes along a K-major row, or 32 K rows of 128 B of an
+          // MN-major tile (encoded >> 4).
+          const uint32_t a_off = A_MN ? (uint32_t)(kk * UMMA_K * 128 >> 4) : (uint32_t)(kk * UMMA_K >> 4);
+          const uint32_t b_off = B_MN ? (uint32_t)(kk * UMMA_K * 128 >> 4) : (uint32_t)(kk * UMMA_K >> 4);
+          if (!(kProfiling && (p.debug_flags & 2)))
+            umma_f8_elect<PAIR>(d_tmem, a_lo + a_off, a_hi, b_lo + b_off, b_hi, IDESC, (kk > 0 || !fresh) ? 1u : 0u);
+        }
+        // smem stage (of both CTAs) free once these MMAs retire
+        umma_commit_elect<PAIR>(bar_empty + 8 * stage);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      };
+      if (p.stages_per_group == 1 && NACC == 2) {
+        // One smem stage per K group (qbk == 128, or K <= 128): a flat loop over
+        // this CTA's (tile, group) sequence, two groups per iteration, so the
+        // accumulator of group j (buffer j & 1, use (j >> 1) + 1) is a constant.
+        const int my_tiles = first_tile < p.num_tiles ? (p.num_tiles - first_tile + tile_step - 1) / tile_step : 0;
+        const int total = my_tiles * p.num_groups;
+        auto group = [&](auto JB, int j) -> bool {
+          constexpr uint32_t buf = decltype(JB)::value;
+          PCB_TRACE(0, j);
+          if (!uwait(bar_tempty + 8 * buf, ((uint32_t)(j >> 1) & 1u) ^ 1u))
+            return false;
+          PCB_TRACE(1, j);
+          if (!uwait(bar_full + 8 * stage, phase)) return false;
+          PCB_TRACE(2, j);
+          issue_stage(tmem_base + buf * BN, true);
+          umma_commit_elect<PAIR>(bar_tfull + 8 * buf);  // accumulator of group j ready (both CTAs)
+          PCB_TRACE(3, j);
+          return true;
+        };
+        for (int j = 0; j < total; j += 2) {
+          if (!group(std::integral_constant<uint32_t, 0>{}, j)) {
             ok = false;
             break;
           }
-          PCB_TRACE(1, acc_cnt);
-          tc_fence_after();
-          const uint32_t d_tmem = tmem_base + abuf * BN;
-          const int ks0 = g * p.stages_per_group;
-          const int ks1 = min(p.k_stages, ks0 + p.stages_per_group);
-          for (int ks = ks0; ks < ks1; ++ks) {
-            if (!wait(bar_full + 8 * stage, phase, SITE_GEMM_MMA)) {
+          if (j + 1 < total && !group(std::integral_constant<uint32_t, 1>{}, j + 1)) {
+            ok = false;
+            break;
+          }
+        }
+      } else {
+        uint32_t acc_cnt = 0;
+        for (int tile = first_tile; tile < p.num_tiles && ok; tile += tile_step) {
+          for (int g = 0; g < p.num_groups && ok; ++g, ++acc_cnt) {
+            const uint32_t abuf = acc_cnt % NACC;
+            PCB_TRACE(0, acc_cnt);
+            if (!uwait(bar_tempty + 8 * abuf, ((acc_cnt / NACC) & 1) ^ 1)) {
               ok = false;
               break;
             }
-            if (ks == ks0) PCB_TRACE(2, acc_cnt);
-            tc_fence_after();
-            const uint32_t sa_addr = s_base + S::OFF_A + stage * S::A_BYTES;
-            const uint32_t sb_addr = s_base + S::OFF_B + stage * S::B_BYTES;
-            const uint64_t adesc0 = make_sw128_desc(sa_addr, A_MN ? (uint32_t)(128 * BK) : 16u);
-            const uint64_t bdesc0 = make_sw128_desc(sb_addr, B_MN ? (uint32_t)(128 * BK) : 16u);
-#pragma unroll
-            for (int kk = 0; kk < BK / UMMA_K; ++kk) {
-              // K advance inside the stage: 32 bytes along a K-major row, or
-              // 32 rows of 128 bytes for an MN-major tile (encoded >> 4).
-              const uint64_t a_off = A_MN ? (uint64_t)(kk * UMMA_K * 128 >> 4) : (uint64_t)(kk * UMMA_K >> 4);
-              const uint64_t b_off = B_MN ? (uint64_t)(kk * UMMA_K * 128 >> 4) : (uint64_t)(kk * UMMA_K >> 4);
-              if (!(kProfiling && (p.debug_flags & 2))) {
-                if constexpr (PAIR) umma_f8_pair(d_tmem, adesc0 + a_off, bdesc0 + b_off, IDESC, (ks > ks0 || kk > 0) ? 1u : 0u);
-                else umma_f8(d_tmem, adesc0 + a_off, bdesc0 + b_off, IDESC, (ks > ks0 || kk > 0) ? 1u : 0u);
+            PCB_TRACE(1, acc_cnt);
+            const int ks0 = g * p.stages_per_group;
+            const int ks1 = min(p.k_stages, ks0 + p.stages_per_group);
+            for (int ks = ks0; ks < ks1; ++ks) {
+              if (!uwait(bar_full + 8 * stage, phase)) {
+                ok = false;
+                break;
               }
+              if (ks == ks0) PCB_TRACE(2, acc_cnt);
+              issue_stage(tmem_base + abuf * BN, ks == ks0);
             }
-            // smem stage (of both CTAs) free once these MMAs retire
-            if constexpr (PAIR) umma_commit_pair(bar_empty + 8 * stage);
-            else umma_commit(bar_empty + 8 * stage);
-            if (++stage == STAGES) {
-              stage = 0;
-              phase ^= 1;
-            }
+            if (!ok) break;
+            umma_commit_elect<PAIR>(bar_tfull + 8 * abuf);  // accumulator of group g ready (both CTAs)
+            PCB_TRACE(3, acc_cnt);
           }
-          if (!ok) break;
-          // accumulator of group g ready (in both CTAs' TMEM)
-          if constexpr (PAIR) umma_commit_pair(bar_tfull + 8 * abuf);
-          else umma_commit(bar_tfull + 8 * abuf);
-          PCB_TRACE(3, acc_cnt);
-          ++acc_cnt;
         }
+      }
+    }
+  } else {
+    // ----------------------------- scale loader --------------------------------
+    // Warps 2-3 stage the fp32 scales of the next W K groups of each tile in
+    // a two-slot shared ring: row scales [g][row] of this CTA's BM rows and,
+    // for uniform B scales, the scale of each epilogue half [g][half].  The
+    // epilogue then reads one shared word per group instead of issuing a
+    // global load whose latency under the operand stream stalls it.
+    const int t = threadIdx.x - 64;
+    uint32_t wc = 0;
+    bool ok = true;
+    for (int tile = first_tile; tile < p.num_tiles && ok; tile += tile_step) {
+      const int b = tile / tiles_per_batch;
+      const int rem = tile - b * tiles_per_batch;
+      const int mb = rem / p.n_blocks;
+      const int nb = rem - mb * p.n_blocks;
+      const int row0 = mb * TILE_M + (int)rank * BM;
+      const float* sa_b = p.sa ? p.sa + (long long)b * p.ssab : nullptr;
+      const float* sb_b = p.sb ? p.sb + (long long)b * p.ssbb : nullptr;
+      for (int g0 = 0; g0 < p.num_groups; g0 += W, ++wc) {
+        const uint32_t slot = wc & 1;
+        if (!mbar_spin_bounded_warp(bar_sempty + 8 * slot, ((wc >> 1) & 1) ^ 1, abort_flag, SITE_GEMM_EPILOGUE)) {
+          ok = false;
+          break;
+        }
+        float* dst = sring + slot * S::SC_SLOT;
+        // Element e = r + BM * gw (rows fastest: conflict-free shared stores);
+        // thread t takes e = t + 64 i, in passes of 4 loads in flight.
+        constexpr int PER_T = BM * W / kScaleThreads, PASS = 4;
+#pragma unroll 1
+        for (int i0 = 0; i0 < PER_T; i0 += PASS) {
+          float v[PASS];
+#pragma unroll
+          for (int i = 0; i < PASS; ++i) {
+            const int e = t + (i0 + i) * kScaleThreads;
+            const int row = row0 + e % BM, g = g0 + e / BM;
+            v[i] = (sa_b && row < p.m && g < p.num_groups)
+                       ? __ldg(sa_b + (long long)(row / p.qbm) * p.ssam + (long long)g * p.ssak)
+                       : 1.f;
+          }
+#pragma unroll
+          for (int i = 0; i < PASS; ++i) dst[t + (i0 + i) * kScaleThreads] = v[i];
+        }
+        if (COL_UNIFORM && t < 2 * W) {
+          const int g = g0 + (t >> 1);
+          const int col = nb * BN + (t & 1) * EPI_COLS;
+          dst[BM * W + t] = (sb_b && col < p.n && g < p.num_groups)
+                                ? __ldg(sb_b + (long long)g * p.ssbk + (long long)(col / p.qbn) * p.ssbn)
+                                : 1.f;
+        }
+        mbar_arrive(bar_sfull + 8 * slot);
       }
     }
   }
@@ -656,6 +757,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* colscale = reinterpret_cast<float*>(smem + S::OFF_COLSCALE) + ew * EPI_COLS;
     const uint32_t colscale_s = smem_u32(colscale);
     uint32_t acc_cnt = 0;
+    uint32_t wc = 0;  // scale windows consumed
     bool ok = true;
     // The tmem-empty barrier lives in the leader; the follower arrives remotely.
     const uint32_t bar_tempty_l = PAIR ? mapa_shared(bar_tempty, 0) : bar_tempty;
@@ -666,22 +768,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int nb = rem - mb * p.n_blocks;
       const int row = mb * TILE_M + (int)rank * BM + row_in_tile;
       const int col0 = nb * BN + half * EPI_COLS;
-      const bool row_ok = row < p.m;
-      const float* sa_row = p.sa ? p.sa + (long long)b * p.ssab + (long long)(row / p.qbm) * p.ssam : nullptr;
       const float* sb_b = p.sb ? p.sb + (long long)b * p.ssbb : nullptr;
 
       float2 acc[EPI_COLS / 2];
 #pragma unroll
       for (int i = 0; i < EPI_COLS / 2; ++i) acc[i] = make_float2(0.f, 0.f);
 
-      auto row_scale = [&](int g) -> float {
-        return (sa_row && row_ok) ? __ldg(sa_row + (long long)g * p.ssak) : 1.f;
-      };
-      auto col_scale = [&](int g) -> float {
-        return (COL_UNIFORM && sb_b && col0 < p.n)
-                   ? __ldg(sb_b + (long long)g * p.ssbk + (long long)(col0 / p.qbn) * p.ssbn)
-                   : 1.f;
-      };
       // Per-column scales (non-uniform B scales): lane l holds columns
       // col0 + 32 q + l of the next K group.
       float cnx[EPI_COLS / 32];
@@ -695,23 +787,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       };
       if constexpr (!COL_UNIFORM) load_cols(0);
-      // The scales of the next two K groups are in flight in registers
-      // (shifted down each group).  The group loop is not unrolled: its
-      // body already holds the 128 accumulators and a 64-column TMEM load.
-      float rs0 = row_scale(0), cs0 = col_scale(0);
-      float rs1 = (1 < p.num_groups) ? row_scale(1) : 1.f, cs1 = (1 < p.num_groups) ? col_scale(1) : 1.f;
-#pragma unroll 1
+      // Pair tiles with uniform B scales: two groups per loop iteration (the
+      // loop-back of a single group costs ~200 cycles of the ~750 a group
+      // takes on the epilogue's critical path).  The other variants keep one
+      // group per iteration, which their registers need.
+#pragma unroll(PAIR && COL_UNIFORM ? 2 : 1)
       for (int g = 0; g < p.num_groups && ok; ++g) {
         {
           const uint32_t abuf = acc_cnt % NACC;
           const uint32_t aphase = (acc_cnt / NACC) & 1;
-          const float s_row = rs0;
-          const float s_col = cs0;
-          rs0 = rs1;
-          cs0 = cs1;
-          if (g + 2 < p.num_groups) {
-            rs1 = row_scale(g + 2);
-            cs1 = col_scale(g + 2);
+          const int gw = g % W;
+          const uint32_t slot = wc & 1;
+          if (gw == 0 && !mbar_spin_bounded_warp(bar_sfull + 8 * slot, (wc >> 1) & 1, abort_flag, SITE_GEMM_EPILOGUE)) {
+            ok = false;
+            break;
+          }
+          const float* ws = sring + slot * S::SC_SLOT;
+          const float s_row = ws[gw * BM + row_in_tile];
+          const float s_col = COL_UNIFORM ? ws[BM * W + gw * 2 + half] : 1.f;
+          if (gw == W - 1 || g + 1 == p.num_groups) {
+            // This warp has read the window's scales.
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_sempty + 8 * slot);
+            ++wc;
           }
           if constexpr (!COL_UNIFORM) {
             // Publish this group's column scales (loaded one group ahead) to
@@ -723,7 +821,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             load_cols(g + 1);
           }
           if (threadIdx.x == 128) PCB_TRACE(4, acc_cnt);
-          if (!wait(bar_tfull + 8 * abuf, aphase, SITE_GEMM_EPILOGUE)) {
+          if (!(PAIR ? mbar_spin_bounded_warp(bar_tfull + 8 * abuf, aphase, abort_flag, SITE_GEMM_EPILOGUE)
+                     : wait(bar_tfull + 8 * abuf, aphase, SITE_GEMM_EPILOGUE))) {
             ok = false;
             break;
           }
@@ -825,6 +924,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  PCB_CTA_SPAN(1);
   tc_fence_before();
   if constexpr (PAIR) {
     cluster_sync_all();  // no CTA leaves while its peer may still touch its smem / barriers
