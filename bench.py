@@ -104,63 +104,76 @@ def profile_json(name: str):
 
 # ------------------------------------------------------------------ clocks ---
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    """SM clock and clock-event (throttle) reasons sampled through NVML every
+    5 ms on a background thread while the timed region runs (nvidia-smi's
+    200 ms floor gives one or two samples of a ~30 ms region)."""
 
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    PERIOD_S = 0.005
+    # NVML clocks-event reason bits -> the names nvidia-smi uses.
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
     def __init__(self, device_index: int):
         self.device_index = device_index
-        self.proc = None
-        self.lines: list[str] = []
+        self.samples: list[tuple[float, float, int]] = []  # (host time, SM MHz, reasons)
+        self.window = None
+        self.sm_max = None
+        self.error = None
+        self._stop = threading.Event()
         self.thread = None
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.device_index), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+            import pynvml
+
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.device_index)
+            self.sm_max = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+        except Exception as exc:  # noqa: BLE001 - no NVML: report why
+            self.error = f"nvml unavailable: {exc}"
             return
-        self.thread = threading.Thread(target=self._read, daemon=True)
+
+        def run():
+            while not self._stop.is_set():
+                try:
+                    sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                    rs = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(h))
+                    self.samples.append((time.perf_counter(), sm, rs))
+                except Exception as exc:  # noqa: BLE001
+                    self.error = str(exc)
+                    return
+                time.sleep(self.PERIOD_S)
+
+        self.thread = threading.Thread(target=run, daemon=True)
         self.thread.start()
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def mark(self, begin: bool) -> None:
+        """Host time of the start / end of the timed region (samples outside it are dropped)."""
+        t = time.perf_counter()
+        self.window = (t, None) if begin else (self.window[0] if self.window else t, t)
 
     def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
+        self._stop.set()
         if self.thread:
             self.thread.join(timeout=2)
-        sm, smax, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 7:
-                continue
-            try:
-                sm.append(float(parts[0]))
-                smax.append(float(parts[1]))
-            except ValueError:
-                continue
-            for nm, v in zip(names, parts[3:7]):
-                if v.lower() == "active":
-                    reasons.add(nm)
+        if self.window and self.window[1] is not None:
+            inside = [x for x in self.samples if self.window[0] <= x[0] <= self.window[1]]
+            self.samples = inside or self.samples
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.sm_max, "reasons": [self.error or "no samples"], "samples": 0}
+        reasons = set()
+        for _, _, rs in self.samples:
+            for bit, name in self.REASONS.items():
+                if rs & bit:
+                    reasons.add(name)
+        sm = [c for _, c, _ in self.samples]
         return {
-            "sm_mhz": statistics.median(sm) if sm else None,
-            "sm_max_mhz": max(smax) if smax else None,
+            "sm_mhz": statistics.median(sm),
+            "sm_max_mhz": self.sm_max,
+            "sm_mhz_min": min(sm),
             "reasons": sorted(reasons),
             "samples": len(sm),
+            "source": f"NVML every {self.PERIOD_S * 1e3:.0f} ms during the timed region",
         }
 
 
@@ -214,12 +227,20 @@ class Dist:
 _FLUSH = {}
 
 
+SPIN_CYCLES = 400_000  # ~200 us at 2 GHz
+
+
 def flush_l2(device) -> None:
-    """Overwrite a buffer twice the L2 size so the next kernel starts cold."""
+    """Read a buffer twice the L2 size so the next kernel starts cold.
+
+    A read sweep evicts every line (dirty lines of earlier kernels are
+    written back during the sweep) and leaves L2 holding clean lines only;
+    a write sweep would leave up to an L2 of dirty lines whose write-backs
+    then compete with the timed kernel's own DRAM traffic."""
     buf = _FLUSH.get(device)
     if buf is None:
-        buf = _FLUSH[device] = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=device)
-    buf.zero_()
+        buf = _FLUSH[device] = torch.zeros(2 * L2_BYTES // 4, dtype=torch.float32, device=device)
+    buf.sum()
 
 
 def time_cold(fn, device, reps: int, warmup: int = 3) -> float:
@@ -232,6 +253,11 @@ def time_cold(fn, device, reps: int, warmup: int = 3) -> float:
     times = []
     for _ in range(reps):
         flush_l2(device)
+        # A GPU-side spin between the flush and the start event gives the host
+        # time to enqueue fn's launches, so the events bracket the kernels and
+        # not the Python wrapper's launch latency (tens of microseconds, the
+        # size of a small quantizer).
+        torch.cuda._sleep(SPIN_CYCLES)
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record(stream)
         fn()
@@ -453,12 +479,17 @@ def run_cfg3(args, d: Dist, local_rank: int, peaks: dict) -> dict:
     torch.cuda.synchronize(device)
     d.barrier()
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if clocks:
+        clocks.mark(True)
+    torch.cuda._sleep(SPIN_CYCLES)  # the first step's launches are queued before the start event
     t_start.record(stream)
     for _ in range(args.steps):
         qa = qb = None
         qa, qb = step(record=True)
     t_end.record(stream)
     torch.cuda.synchronize(device)
+    if clocks:
+        clocks.mark(False)
     d.barrier()
     clock_info = clocks.stop() if clocks else None
     elapsed_ms = t_start.elapsed_time(t_end)
@@ -581,6 +612,11 @@ def run_cfg3(args, d: Dist, local_rank: int, peaks: dict) -> dict:
             frac_vs_cublaslt_fp8_in_run=(achieved / cublas_fp8) if cublas_fp8 else None,
             cublaslt_fp8_tflops_in_run=cublas_fp8,
             frac_vs_4500_spec=achieved / 4500.0,
+            # A kernel timed inside a long back-to-back loop runs power-capped
+            # (see `clocks`); the driver's sustained bf16 loop is that regime.
+            peak_sustained=2 * peaks["bf16_tflops_sustained"] if peaks.get("bf16_tflops_sustained") else None,
+            frac_vs_sustained=(achieved / (2 * peaks["bf16_tflops_sustained"]))
+            if peaks.get("bf16_tflops_sustained") else None,
             traffic_source=(tr or {}).get("source")),
         "roofline_quant_a": roofline(
             "hbm", qa_bytes / (qa_ms * 1e-3) / 1e9, peaks["hbm_gbs"], "GB/s",
@@ -717,6 +753,7 @@ def run_cfg4(args, d: Dist) -> dict:
         d.barrier()
         reps = 5
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(SPIN_CYCLES)
         s.record(stream)
         for _ in range(reps):
             quant_bmm_fused(x, qw, out=out, fuse=fuse)

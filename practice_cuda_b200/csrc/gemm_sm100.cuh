@@ -70,10 +70,13 @@ __device__ long long g_gemm_trace[16][1024];
   do {                                                                       \
     if (blockIdx.x == 0 && (idx) < 1024) g_gemm_trace[ev][idx] = clock64(); \
   } while (0)
-__device__ unsigned long long g_cta_span[2][1024];  // per-CTA start / end (globaltimer ns)
-#define PCB_CTA_SPAN(i) \
-  do {                  \
-    if (threadIdx.x == 0 && blockIdx.x < 1024) g_cta_span[i][blockIdx.x] = global_timer_ns(); \
+__device__ unsigned long long g_cta_span[4][1024];  // per-CTA start / end: globaltimer ns, clock64
+#define PCB_CTA_SPAN(i)                                        \
+  do {                                                         \
+    if (threadIdx.x == 0 && blockIdx.x < 1024) {               \
+      g_cta_span[i][blockIdx.x] = global_timer_ns();           \
+      g_cta_span[2 + (i)][blockIdx.x] = (unsigned long long)clock64(); \
+    }                                                          \
   } while (0)
 #else
 #define PCB_TRACE(ev, idx) \

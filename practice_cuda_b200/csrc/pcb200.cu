@@ -58,6 +58,14 @@ DeviceInfo device_info() {
 
 bool aligned(const void* p, int64_t a) { return (reinterpret_cast<uintptr_t>(p) % (uintptr_t)a) == 0; }
 
+template <typename K>
+void ensure_smem_attr(K kernel, int bytes) {
+  // cudaFuncSetAttribute is per function and device; calling it again is cheap
+  // and keeps this stateless across devices and threads.
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+
 int elem_size(int dt) {
   switch (dt) {
     case PCB_DTYPE_F32: return 4;
@@ -220,30 +228,23 @@ int launch_groups(const void* x, int xt, int64_t batch, int64_t m, int64_t n, in
         kernel<<<(unsigned)grid, quant::kThreads, 0, stream>>>(a);
         return check_launch("quant_groups_kernel");
       };
-      if (mode == quant::kDeqPow2) {
-        if (nch <= 16) return go(quant::quant_groups_kernel<XT, YT, 8, 2, quant::kDeqPow2>, 8);
-        if (nch <= 32) return go(quant::quant_groups_kernel<XT, YT, 16, 2, quant::kDeqPow2>, 16);
-        if (nch <= 128) return go(quant::quant_groups_kernel<XT, YT, 32, 4, quant::kDeqPow2>, 32);
-        return go(quant::quant_groups_kernel<XT, YT, 256, 8, quant::kDeqPow2>, 256);
-      }
-      if (quant_divide) {
-        constexpr int Q = quant::kQuantDivide;
-        if (nch <= 16) return go(quant::quant_groups_kernel<XT, YT, 8, 2, Q>, 8);
-        if (nch <= 32) return go(quant::quant_groups_kernel<XT, YT, 16, 2, Q>, 16);
-        if (nch <= 128) return go(quant::quant_groups_kernel<XT, YT, 32, 4, Q>, 32);
-        return go(quant::quant_groups_kernel<XT, YT, 256, 8, Q>, 256);
-      }
-      if (mode == quant::kDeqReciprocal) {
-        if (nch <= 16) return go(quant::quant_groups_kernel<XT, YT, 8, 2, quant::kDeqReciprocal>, 8);
-        if (nch <= 32) return go(quant::quant_groups_kernel<XT, YT, 16, 2, quant::kDeqReciprocal>, 16);
-        if (nch <= 128) return go(quant::quant_groups_kernel<XT, YT, 32, 4, quant::kDeqReciprocal>, 32);
-        return go(quant::quant_groups_kernel<XT, YT, 256, 8, quant::kDeqReciprocal>, 256);
-      } else {
-        if (nch <= 16) return go(quant::quant_groups_kernel<XT, YT, 8, 2, quant::kDeqDivide>, 8);
-        if (nch <= 32) return go(quant::quant_groups_kernel<XT, YT, 16, 2, quant::kDeqDivide>, 16);
-        if (nch <= 128) return go(quant::quant_groups_kernel<XT, YT, 32, 4, quant::kDeqDivide>, 32);
-        return go(quant::quant_groups_kernel<XT, YT, 256, 8, quant::kDeqDivide>, 256);
-      }
+      // Team size and 16-byte chunks per thread by group size: groups of up
+      // to 512 chunks (4096 bf16, a per-channel row) take one warp with up to
+      // 16 loads in flight per lane and a shuffle reduction; larger groups a
+      // whole CTA.
+      auto by_size = [&](auto mc) -> int {
+        constexpr int MODE = decltype(mc)::value;
+        if (nch <= 16) return go(quant::quant_groups_kernel<XT, YT, 8, 2, MODE>, 8);
+        if (nch <= 32) return go(quant::quant_groups_kernel<XT, YT, 16, 2, MODE>, 16);
+        if (nch <= 128) return go(quant::quant_groups_kernel<XT, YT, 32, 4, MODE>, 32);
+        if (nch <= 256) return go(quant::quant_groups_kernel<XT, YT, 32, 8, MODE>, 32);
+        if (nch <= 512) return go(quant::quant_groups_kernel<XT, YT, 32, 16, MODE>, 32);
+        return go(quant::quant_groups_kernel<XT, YT, 256, 8, MODE>, 256);
+      };
+      if (mode == quant::kDeqPow2) return by_size(std::integral_constant<int, quant::kDeqPow2>{});
+      if (quant_divide) return by_size(std::integral_constant<int, quant::kQuantDivide>{});
+      if (mode == quant::kDeqReciprocal) return by_size(std::integral_constant<int, quant::kDeqReciprocal>{});
+      return by_size(std::integral_constant<int, quant::kDeqDivide>{});
     });
   }
   if (mode == quant::kDeqPow2)
@@ -298,13 +299,6 @@ bool make_map_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t ou
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
-}
-
-template <typename K>
-void ensure_smem_attr(K kernel, int bytes) {
-  // cudaFuncSetAttribute is per function and device; calling it again is cheap
-  // and keeps this stateless across devices and threads.
-  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
 // 3-D map of 16-bit elements (inner, outer, batch), unswizzled box (128, 128, 1):

@@ -197,14 +197,23 @@ __global__ void __launch_bounds__(kThreads) quant_groups_kernel(const GroupArgs 
 
     C reg[CH];
     uint32_t amax = 0;
+    if (nch == CH * TEAM && cpr == nch) {
+      // A full single-row group: all CH loads issue before any of them is
+      // used (per-chunk bounds checks would keep them in program order).
 #pragma unroll
-    for (int i = 0; i < CH; ++i) {
-      const int c = i * TEAM + t;
-      if (c < nch) {
-        const int r = c / cpr;
-        const int cc = c - r * cpr;
-        reg[i].load(xg + r * args.sxm + cc * VEC);
-        amax = max(amax, reg[i].amax_bits());
+      for (int i = 0; i < CH; ++i) reg[i].load(xg + (i * TEAM + t) * VEC);
+#pragma unroll
+      for (int i = 0; i < CH; ++i) amax = max(amax, reg[i].amax_bits());
+    } else {
+#pragma unroll
+      for (int i = 0; i < CH; ++i) {
+        const int c = i * TEAM + t;
+        if (c < nch) {
+          const int r = c / cpr;
+          const int cc = c - r * cpr;
+          reg[i].load(xg + r * args.sxm + cc * VEC);
+          amax = max(amax, reg[i].amax_bits());
+        }
       }
     }
     for (int c = CH * TEAM + t; c < nch; c += TEAM) {  // groups larger than the register tile
@@ -389,8 +398,12 @@ struct ColArgs {
 //               rows split over a cluster, dequant = amax / fp8_max).
 // SLAB = true:  per-block (rows_per_cta x 1) blocks, e.g. 128 x 1: CTA
 //               blockIdx.y owns one row slab, dequant = 1 / quant_scale.
+// Both passes over the slab (amax, then the cast, whose re-read hits L2) take
+// the thread's rows kUnroll at a time with the loads issued first, so a CTA
+// keeps kUnroll 16-byte loads per thread in flight.
+constexpr int kColUnroll = 6;
 template <int XT, int YT, bool SLAB = false, int MODE = kDeqReciprocal>
-__global__ void __launch_bounds__(kThreads) quant_cols_cluster_kernel(const ColArgs args) {
+__global__ void __launch_bounds__(kThreads, 4) quant_cols_cluster_kernel(const ColArgs args) {
   using C = Chunk<XT>;
   using T = typename C::T;
   constexpr int VEC = C::VEC;
@@ -420,15 +433,39 @@ __global__ void __launch_bounds__(kThreads) quant_cols_cluster_kernel(const ColA
   const T* xb = static_cast<const T*>(args.x) + b * args.sxb;
   uint8_t* yb = static_cast<uint8_t*>(args.y) + b * args.syb;
 
+  // Column amax as ordered magnitude bits.  16-bit inputs keep two columns
+  // per word and reduce them with packed unsigned 16-bit max (NaN compares
+  // above inf), widened to fp32 bits once at the end.
   uint32_t am[VEC];
+  uint32_t am2[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
   for (int i = 0; i < VEC; ++i) am[i] = 0;
   if (col_ok) {
-    for (int64_t r = r_begin + rl; r < r_end; r += ROW_LANES) {
-      C ch;
-      ch.load(xb + r * args.sxm + col);
+    for (int64_t r0 = r_begin + rl; r0 < r_end; r0 += (int64_t)kColUnroll * ROW_LANES) {
+      C ch[kColUnroll];
 #pragma unroll
-      for (int i = 0; i < VEC; ++i) am[i] = max(am[i], abs_bits(ch.v(i)));
+      for (int j = 0; j < kColUnroll; ++j) {
+        const int64_t r = r0 + (int64_t)j * ROW_LANES;
+        if (r < r_end) ch[j].load(xb + r * args.sxm + col);
+        else ch[j].raw = make_uint4(0u, 0u, 0u, 0u);  // |0| leaves the amax unchanged
+      }
+#pragma unroll
+      for (int j = 0; j < kColUnroll; ++j) {
+        if constexpr (XT == PCB_DTYPE_F32) {
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) am[i] = max(am[i], abs_bits(ch[j].v(i)));
+        } else {
+#pragma unroll
+          for (int w = 0; w < 4; ++w) am2[w] = __vmaxu2(am2[w], ch[j].word(w) & 0x7fff7fffu);
+        }
+      }
+    }
+  }
+  if constexpr (XT != PCB_DTYPE_F32) {
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      am[2 * w] = C::bits16_to_f32_bits(am2[w] & 0xffffu);
+      am[2 * w + 1] = C::bits16_to_f32_bits(am2[w] >> 16);
     }
   }
 #pragma unroll
@@ -466,23 +503,37 @@ __global__ void __launch_bounds__(kThreads) quant_cols_cluster_kernel(const ColA
   } else {
     cg::this_cluster().sync();  // remote reads of `partial` are done; qs_s visible to the CTA
   }
-  if (col_ok) {
-    for (int64_t r = r_begin + rl; r < r_end; r += ROW_LANES) {
-      C ch;
-      ch.load(xb + r * args.sxm + col);
-      // Chunk::store takes one scale; columns differ, so convert pairwise here.
-      uint8_t out[VEC];
+  // This thread's column scales, read from shared memory once.
+  float qreg[VEC];
 #pragma unroll
-      for (int i = 0; i < VEC; i += 2) {
-        const uint16_t p = cvt2_fp8<YT>(__fmul_rn(ch.v(i), qs_s[cc * VEC + i]),
-                                        __fmul_rn(ch.v(i + 1), qs_s[cc * VEC + i + 1]));
-        out[i] = (uint8_t)(p & 0xff);
-        out[i + 1] = (uint8_t)(p >> 8);
+  for (int i = 0; i < VEC; ++i) qreg[i] = qs_s[cc * VEC + i];
+  // Chunk::store takes one scale; columns differ, so convert pairwise here.
+  auto cast_store = [&](const C& ch, int64_t r) {
+    uint8_t out[VEC];
+#pragma unroll
+    for (int i = 0; i < VEC; i += 2) {
+      const uint16_t p = cvt2_fp8<YT>(__fmul_rn(ch.v(i), qreg[i]), __fmul_rn(ch.v(i + 1), qreg[i + 1]));
+      out[i] = (uint8_t)(p & 0xff);
+      out[i + 1] = (uint8_t)(p >> 8);
+    }
+    if constexpr (VEC == 8) {
+      *reinterpret_cast<uint2*>(yb + r * args.sym + col) = *reinterpret_cast<const uint2*>(out);
+    } else {
+      *reinterpret_cast<uint32_t*>(yb + r * args.sym + col) = *reinterpret_cast<const uint32_t*>(out);
+    }
+  };
+  if (col_ok) {
+    for (int64_t r0 = r_begin + rl; r0 < r_end; r0 += (int64_t)kColUnroll * ROW_LANES) {
+      C ch[kColUnroll];
+#pragma unroll
+      for (int j = 0; j < kColUnroll; ++j) {
+        const int64_t r = r0 + (int64_t)j * ROW_LANES;
+        if (r < r_end) ch[j].load(xb + r * args.sxm + col);
       }
-      if constexpr (VEC == 8) {
-        *reinterpret_cast<uint2*>(yb + r * args.sym + col) = *reinterpret_cast<const uint2*>(out);
-      } else {
-        *reinterpret_cast<uint32_t*>(yb + r * args.sym + col) = *reinterpret_cast<const uint32_t*>(out);
+#pragma unroll
+      for (int j = 0; j < kColUnroll; ++j) {
+        const int64_t r = r0 + (int64_t)j * ROW_LANES;
+        if (r < r_end) cast_store(ch[j], r);
       }
     }
   }

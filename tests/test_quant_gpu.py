@@ -185,3 +185,22 @@ def test_per_block_pow2_vs_oracle(dtype, shape, bm, bn):
     s = q.dequant_scale.cpu()
     assert torch.equal(torch.frexp(s).mantissa, torch.full_like(s, 0.5))
     assert q.meta["scale_format"] == "e8m0"
+
+
+# Per-channel rows through the one-warp-per-row kernel (rows of up to 512
+# 16-byte chunks) and the CTA-per-row kernel beyond: every input dtype, both
+# fp8 formats, row counts that leave a partial CTA, a batched (3-D) input,
+# an all-zero row.
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("fp8", [E4M3, E5M2])
+@pytest.mark.parametrize("shape", [(13, 512), (1001, 4096), (3, 77, 2048), (64, 1000), (9, 8192)])
+def test_per_channel_rows_vs_oracle(dtype, fp8, shape):
+    es = torch.tensor([], dtype=dtype).element_size()
+    if shape[-1] * es > 8192 and dtype != torch.bfloat16:
+        pytest.skip("one length beyond 512 chunks is enough")
+    x = synthetic(shape, dtype=dtype, outliers=True, seed=7)
+    x[..., 3, :] = 0  # an all-zero row: amax clamps to eps
+    q = get_quant("b200_per_channel").fn(x.to(DEV), channel_axis=-2, fp8_dtype=fp8)
+    y_ref, s_ref = oracle.per_channel_quant(x, channel_axis=-2, fp8_dtype=fp8)
+    assert_bytes_equal(q.tensor, y_ref, f"rows {dtype} {shape}")
+    assert_scales_equal(q.dequant_scale, s_ref, f"rows scales {dtype} {shape}")
