@@ -50,9 +50,7 @@ struct FusedSmem {
   static constexpr int ALLOC = BYTES + 1024;
 };
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
+
 
 template <bool B_MN, int XT, bool COL_UNIFORM>
 __global__ void __launch_bounds__(kFusedThreads, 1)

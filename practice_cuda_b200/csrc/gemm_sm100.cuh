@@ -7,7 +7,7 @@
 //   warp 1      TMEM allocator + MMA issuer (warp-uniform loop, elect.sync
 //               lane issues)
 //   warps 2-3   scale loader: each tile's fp32 scales, W K groups at a time,
-//               into a two-slot shared ring read by the epilogue
+//               into a four-slot shared ring read by the epilogue
 //   warps 4-11  epilogue: two warpgroups; warpgroup h owns tile columns
 //               [h*BN/2, (h+1)*BN/2), warp (w % 4) owns TMEM lanes / rows
 //               [32*(w%4), 32*(w%4)+32).
@@ -52,6 +52,7 @@ static_assert(128 * kLowRegs + 256 * kHighRegs == kThreads * kLaunchRegs, "regis
 #endif
 constexpr int kNumAcc = 4;        // TMEM accumulator buffers of BN fp32 columns
 constexpr int kScaleWin = 8;      // K groups of scales per shared-memory window
+constexpr int kScaleSlots = 4;    // windows in the shared-memory scale ring
 constexpr int kScaleThreads = 64; // scale-loader threads (warps 2-3)
 
 // Profiling switches (Params::debug_flags) exist only in builds compiled with
@@ -107,6 +108,7 @@ struct Params {
   long long scb, scm;
   int c_dtype;
   int c_vec;  // 16-byte vector stores allowed
+  int c_tma;  // bf16 / fp16 C written by TMA stores from shared memory (bmm_scaled_kernel on a CTA pair)
   const void* bias;
   long long sbib, sbim, sbin;
   int bias_dtype;
@@ -363,7 +365,8 @@ template <int BN, bool PAIR = false>
 struct Smem {
   // A CTA pair splits the B tile: each CTA stages BN/2 of its N rows.
   static constexpr int B_ROWS = PAIR ? BN / 2 : BN;
-  static constexpr int STAGES = (BN == 256 && !PAIR) ? 4 : 6;
+  // The CTA pair gives one operand stage (32 KB) to output staging.
+  static constexpr int STAGES = (BN == 256 && !PAIR) ? 4 : (PAIR ? 5 : 6);
   static constexpr int A_BYTES = BM * BK;      // 16 KB
   static constexpr int B_BYTES = B_ROWS * BK;  // 32 / 16 KB
   static constexpr int EPI_COLS = BN / 2;
@@ -373,12 +376,37 @@ struct Smem {
   // Scale ring slot: row scales [kScaleWin][BM], then uniform B scales [kScaleWin][2].
   static constexpr int SC_SLOT = kScaleWin * (BM + 2);
   static constexpr int OFF_SCALE = OFF_COLSCALE + 8 * EPI_COLS * 4;
-  static constexpr int OFF_BAR = OFF_SCALE + 2 * SC_SLOT * 4;
-  static constexpr int NUM_BARS = 2 * STAGES + 2 * kNumAcc + 4;
+  static constexpr int OFF_BAR = OFF_SCALE + kScaleSlots * SC_SLOT * 4;
+  static constexpr int NUM_BARS = 2 * STAGES + 2 * kNumAcc + 2 * kScaleSlots;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;                  // tmem addr, abort flag
-  static constexpr int BYTES = OFF_MISC + 16;
+  // Output staging for TMA stores (CTA pair only): one 4 KB buffer per
+  // epilogue warp, a 32-row x 64-column bf16 / fp16 box in the 128-byte swizzle.
+  static constexpr int CSTG_BUF = PAIR ? 4096 : 0;
+  static constexpr int OFF_CSTG = (OFF_MISC + 16 + 1023) / 1024 * 1024;
+  static constexpr int BYTES = OFF_CSTG + 8 * CSTG_BUF;
   static constexpr int ALLOC = BYTES + 1024;                              // slack for 1 KB alignment
+  static_assert(ALLOC <= 232448, "shared memory per CTA");
 };
+
+// TMA store of one box from shared memory, tracked in this thread's bulk groups.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Wait until at most N of this thread's bulk store groups still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+// Generic-proxy shared-memory writes become visible to the async (TMA) proxy.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.7071067811865475f)); }
 
@@ -462,10 +490,65 @@ __device__ __forceinline__ void store_row(const Params& p, float* accf, int b, i
   }
 }
 
+// Bias, activation and a TMA store of one warp's 32 rows x EPI_COLS columns
+// of bf16 / fp16 C, 64 columns at a time: every lane writes its row's 128
+// bytes into the warp's 4 KB staging buffer (128-byte swizzle: conflict-free)
+// and lane 0 stores the 32 x 64 box.  Whole 128-byte row segments keep the
+// store engine's request count low (per-thread 16-byte row stores cost ~9000
+// cycles per 256 x 256 tile, during which the MMA stalls).  The buffer is
+// rewritten only after the previous box store has read it.  Rows and columns
+// outside C are clipped by the tensor map.
+template <int EPI_COLS>
+__device__ __forceinline__ void store_rows_tma(const Params& p, const CUtensorMap* tmap_c, float* accf, int b,
+                                               int row, int warp_row0, int col0, uint32_t stg, int lane) {
+  if (row < p.m) {
+    if (p.bias) {
+#pragma unroll
+      for (int i = 0; i < EPI_COLS; ++i) {
+        const int c = col0 + i;
+        if (c < p.n)
+          accf[i] += load_bias(p.bias, p.bias_dtype, (long long)b * p.sbib + (long long)row * p.sbim + (long long)c * p.sbin);
+      }
+    }
+    if (p.activation == PCB_ACT_GELU) {
+#pragma unroll
+      for (int i = 0; i < EPI_COLS; ++i) accf[i] = gelu_erf(accf[i]);
+    }
+  }
+  const bool bf16 = p.c_dtype == PCB_DTYPE_BF16;
+  const uint32_t swz = (uint32_t)(lane & 7);
+#pragma unroll
+  for (int q = 0; q < EPI_COLS / 64; ++q) {
+    if (lane == 0) bulk_wait_read<0>();
+    __syncwarp();
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      uint32_t w[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float lo = accf[64 * q + 8 * c + 2 * j], hi = accf[64 * q + 8 * c + 2 * j + 1];
+        if (bf16) {
+          __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+          w[j] = *reinterpret_cast<uint32_t*>(&h);
+        } else {
+          __half2 h = __floats2half2_rn(lo, hi);
+          w[j] = *reinterpret_cast<uint32_t*>(&h);
+        }
+      }
+      const uint32_t dst = stg + (uint32_t)lane * 128u + (((uint32_t)c ^ swz) << 4);
+      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3])
+                   : "memory");
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0 && warp_row0 < p.m && col0 + 64 * q < p.n) tma_store_3d(tmap_c, stg, col0 + 64 * q, warp_row0, b);
+  }
+}
+
 template <int BN, bool A_MN, bool B_MN, bool COL_UNIFORM, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     bmm_scaled_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                      const Params p) {
+                      const __grid_constant__ CUtensorMap tmap_c, const Params p) {
   static_assert(!PAIR || BN == 256, "the CTA pair runs 256x256 tiles");
   using S = Smem<BN, PAIR>;
   constexpr int STAGES = S::STAGES;
@@ -486,9 +569,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t bar_empty = bar_full + 8 * STAGES;               // [STAGES]
   const uint32_t bar_tfull = bar_empty + 8 * STAGES;              // [NACC]
   const uint32_t bar_tempty = bar_tfull + 8 * kNumAcc;            // [NACC]
-  const uint32_t bar_sfull = bar_tempty + 8 * kNumAcc;            // [2] scale window loaded
-  const uint32_t bar_sempty = bar_sfull + 16;                     // [2] scale window consumed
-  float* sring = reinterpret_cast<float*>(smem + S::OFF_SCALE);   // [2][S::SC_SLOT]
+  const uint32_t bar_sfull = bar_tempty + 8 * kNumAcc;            // [kScaleSlots] scale window loaded
+  const uint32_t bar_sempty = bar_sfull + 8 * kScaleSlots;        // [kScaleSlots] scale window consumed
+  float* sring = reinterpret_cast<float*>(smem + S::OFF_SCALE);   // [kScaleSlots][S::SC_SLOT]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 4);
 
@@ -514,7 +597,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar_tfull + 8 * i, 1);
       mbar_init(bar_tempty + 8 * i, PAIR ? 16 : 8);  // one arrive per epilogue warp (of both CTAs)
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kScaleSlots; ++i) {
       mbar_init(bar_sfull + 8 * i, kScaleThreads);  // every scale-loader thread
       mbar_init(bar_sempty + 8 * i, 8);             // every epilogue warp of this CTA
     }
@@ -700,7 +783,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ----------------------------- scale loader --------------------------------
     // Warps 2-3 stage the fp32 scales of the next W K groups of each tile in
-    // a two-slot shared ring: row scales [g][row] of this CTA's BM rows and,
+    // a four-slot shared ring: row scales [g][row] of this CTA's BM rows and,
     // for uniform B scales, the scale of each epilogue half [g][half].  The
     // epilogue then reads one shared word per group instead of issuing a
     // global load whose latency under the operand stream stalls it.
@@ -716,15 +799,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float* sa_b = p.sa ? p.sa + (long long)b * p.ssab : nullptr;
       const float* sb_b = p.sb ? p.sb + (long long)b * p.ssbb : nullptr;
       for (int g0 = 0; g0 < p.num_groups; g0 += W, ++wc) {
-        const uint32_t slot = wc & 1;
-        if (!mbar_spin_bounded_warp(bar_sempty + 8 * slot, ((wc >> 1) & 1) ^ 1, abort_flag, SITE_GEMM_EPILOGUE)) {
+        const uint32_t slot = wc % kScaleSlots;
+        if (!mbar_spin_bounded_warp(bar_sempty + 8 * slot, ((wc / kScaleSlots) & 1) ^ 1, abort_flag,
+                                    SITE_GEMM_EPILOGUE)) {
           ok = false;
           break;
         }
         float* dst = sring + slot * S::SC_SLOT;
         // Element e = r + BM * gw (rows fastest: conflict-free shared stores);
         // thread t takes e = t + 64 i, in passes of 4 loads in flight.
-        constexpr int PER_T = BM * W / kScaleThreads, PASS = 4;
+        constexpr int PER_T = BM * W / kScaleThreads, PASS = 8;
 #pragma unroll 1
         for (int i0 = 0; i0 < PER_T; i0 += PASS) {
           float v[PASS];
@@ -800,8 +884,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t abuf = acc_cnt % NACC;
           const uint32_t aphase = (acc_cnt / NACC) & 1;
           const int gw = g % W;
-          const uint32_t slot = wc & 1;
-          if (gw == 0 && !mbar_spin_bounded_warp(bar_sfull + 8 * slot, (wc >> 1) & 1, abort_flag, SITE_GEMM_EPILOGUE)) {
+          const uint32_t slot = wc % kScaleSlots;
+          if (gw == 0 &&
+              !mbar_spin_bounded_warp(bar_sfull + 8 * slot, (wc / kScaleSlots) & 1, abort_flag, SITE_GEMM_EPILOGUE)) {
             ok = false;
             break;
           }
@@ -923,8 +1008,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       // Bias, activation, cast, store.
       float* accf = reinterpret_cast<float*>(acc);
-      store_row<EPI_COLS>(p, accf, b, row, col0);
+      if (PAIR && p.c_tma)
+        store_rows_tma<EPI_COLS>(p, &tmap_c, accf, b, row, mb * TILE_M + (int)rank * BM + quarter * 32, col0,
+                                 s_base + S::OFF_CSTG + (uint32_t)(ew * S::CSTG_BUF), lane);
+      else
+        store_row<EPI_COLS>(p, accf, b, row, col0);
     }
+    // The staging buffers stay valid until every issued store has completed.
+    if (PAIR && p.c_tma && lane == 0) bulk_wait_all();
   }
 
   PCB_CTA_SPAN(1);

@@ -319,6 +319,23 @@ bool make_map_x16(CUtensorMap* map, const void* base, int dt, uint64_t inner, ui
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 3-D map of a bf16 / fp16 output C (n, m, batch) for TMA stores of 64-column
+// x 32-row boxes in the 128-byte swizzle (the pair epilogue's staging layout).
+bool make_map_c16(CUtensorMap* map, void* base, int dt, uint64_t n, uint64_t m, uint64_t batch,
+                  uint64_t row_stride_bytes, uint64_t batch_stride_bytes) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {n, m, batch};
+  if (batch <= 1) batch_stride_bytes = std::max<uint64_t>(16, ((m * row_stride_bytes + 15) / 16) * 16);
+  cuuint64_t strides[2] = {row_stride_bytes, batch_stride_bytes};
+  cuuint32_t box[3] = {64, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapDataType t =
+      dt == PCB_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return fn(map, t, 3, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // Unswizzled (128, 128, 1) box of bf16 / fp16 / fp32 elements: one quantizer tile.
 bool make_map_tile(CUtensorMap* map, const void* base, int dt, uint64_t inner, uint64_t outer, uint64_t batch,
                    uint64_t outer_stride_bytes, uint64_t batch_stride_bytes) {
@@ -347,8 +364,8 @@ int launch_fused(const CUtensorMap& tx, const CUtensorMap& tb, const gemm::Param
 
 
 template <int BN, bool A_MN, bool B_MN, bool COLU, bool PAIR>
-int launch_bmm(const CUtensorMap& ta, const CUtensorMap& tb, const gemm::Params& p, int sm_count,
-               cudaStream_t stream) {
+int launch_bmm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const gemm::Params& p,
+               int sm_count, cudaStream_t stream) {
   using S = gemm::Smem<BN, PAIR>;
   auto kernel = gemm::bmm_scaled_kernel<BN, A_MN, B_MN, COLU, PAIR>;
   if constexpr (BN == 256) {
@@ -379,18 +396,19 @@ int launch_bmm(const CUtensorMap& ta, const CUtensorMap& tb, const gemm::Params&
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaLaunchKernelEx(&cfg, kernel, ta, tb, p);
+    cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, p);
   } else {
     const int grid = std::min(p.num_tiles, sm_count);
-    kernel<<<grid, gemm::kThreads, S::ALLOC, stream>>>(ta, tb, p);
+    kernel<<<grid, gemm::kThreads, S::ALLOC, stream>>>(ta, tb, tc, p);
   }
   return check_launch("bmm_scaled_kernel");
 }
 
 template <int BN, bool A_MN, bool B_MN, bool PAIR>
-int launch_bmm_cols(const CUtensorMap& ta, const CUtensorMap& tb, const gemm::Params& p, int sm, cudaStream_t s) {
-  if (p.col_uniform) return launch_bmm<BN, A_MN, B_MN, true, PAIR>(ta, tb, p, sm, s);
-  return launch_bmm<BN, A_MN, B_MN, false, PAIR>(ta, tb, p, sm, s);
+int launch_bmm_cols(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const gemm::Params& p, int sm,
+                    cudaStream_t s) {
+  if (p.col_uniform) return launch_bmm<BN, A_MN, B_MN, true, PAIR>(ta, tb, tc, p, sm, s);
+  return launch_bmm<BN, A_MN, B_MN, false, PAIR>(ta, tb, tc, p, sm, s);
 }
 
 template <bool A_MN, bool B_MN, int FMT>
@@ -426,12 +444,12 @@ int dispatch_bmm_bs(bool a_mn, bool b_mn, int fmt, const CUtensorMap& ta, const 
 }
 
 template <int BN, bool PAIR>
-int dispatch_bmm_layout(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const gemm::Params& p,
-                        int sm, cudaStream_t s) {
-  if (!a_mn && !b_mn) return launch_bmm_cols<BN, false, false, PAIR>(ta, tb, p, sm, s);
-  if (!a_mn && b_mn) return launch_bmm_cols<BN, false, true, PAIR>(ta, tb, p, sm, s);
-  if (a_mn && !b_mn) return launch_bmm_cols<BN, true, false, PAIR>(ta, tb, p, sm, s);
-  return launch_bmm_cols<BN, true, true, PAIR>(ta, tb, p, sm, s);
+int dispatch_bmm_layout(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                        const gemm::Params& p, int sm, cudaStream_t s) {
+  if (!a_mn && !b_mn) return launch_bmm_cols<BN, false, false, PAIR>(ta, tb, tc, p, sm, s);
+  if (!a_mn && b_mn) return launch_bmm_cols<BN, false, true, PAIR>(ta, tb, tc, p, sm, s);
+  if (a_mn && !b_mn) return launch_bmm_cols<BN, true, false, PAIR>(ta, tb, tc, p, sm, s);
+  return launch_bmm_cols<BN, true, true, PAIR>(ta, tb, tc, p, sm, s);
 }
 
 // ---------------------------------------------------------------------------
@@ -983,9 +1001,17 @@ static int bmm_entry(const void* a, int64_t sab, int64_t sam, int64_t sak, const
     p.sfb = sfb;
     return dispatch_bmm_bs(a_mn, b_mn, fmt, ta, tb, p, di.sm_count, s);
   }
-  if (pair) return dispatch_bmm_layout<256, true>(a_mn, b_mn, ta, tb, p, di.sm_count, s);
-  if (bn == 256) return dispatch_bmm_layout<256, false>(a_mn, b_mn, ta, tb, p, di.sm_count, s);
-  return dispatch_bmm_layout<128, false>(a_mn, b_mn, ta, tb, p, di.sm_count, s);
+  // On the CTA pair, bf16 / fp16 C leaves through TMA stores of swizzled
+  // 32 x 64 boxes staged in shared memory (per-thread row stores stall the
+  // epilogue, and with it the MMA, for thousands of cycles per tile).
+  CUtensorMap tc;
+  std::memset(&tc, 0, sizeof(tc));
+  if (pair && (c_dtype == PCB_DTYPE_BF16 || c_dtype == PCB_DTYPE_F16) && p.c_vec)
+    p.c_tma = make_map_c16(&tc, c, c_dtype, (uint64_t)n, (uint64_t)m, (uint64_t)batch, (uint64_t)scm * 2,
+                           (uint64_t)scb * 2) ? 1 : 0;
+  if (pair) return dispatch_bmm_layout<256, true>(a_mn, b_mn, ta, tb, tc, p, di.sm_count, s);
+  if (bn == 256) return dispatch_bmm_layout<256, false>(a_mn, b_mn, ta, tb, tc, p, di.sm_count, s);
+  return dispatch_bmm_layout<128, false>(a_mn, b_mn, ta, tb, tc, p, di.sm_count, s);
 }
 int pcb_bmm_scaled(const void* a, int64_t sab, int64_t sam, int64_t sak, const void* b, int64_t sbb, int64_t sbk,
                    int64_t sbn, int ab_dtype, int64_t batch, int64_t m, int64_t n, int64_t k, const float* scale_a,
