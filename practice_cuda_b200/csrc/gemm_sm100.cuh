@@ -954,26 +954,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                                              s2, acc[c * 16 + i]);
               }
           } else {
-            // Wide half-tile: CW-column TMEM loads, one round trip each
-            // (the TMEM load latency, not the FMAs, bounds this loop); the
+            // Wide half-tile: 32-column TMEM loads, double-buffered so the
+            // load of chunk c + 1 is in flight while chunk c is promoted; the
             // buffer is released as soon as the last load has landed.
-            constexpr int CW = PCB_GEMM_EPI_CW;
+            constexpr int CW = 32;
             constexpr int NCH = EPI_COLS / CW;
-#pragma unroll
-            for (int c = 0; c < NCH; ++c) {
-              uint32_t vc[CW];
-              tmem_ld_n(taddr + c * CW, vc);
-              tmem_wait_ld();
-              tmem_regs_ready(vc);
-              if (c + 1 == NCH) {
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) {
-                  if constexpr (PAIR) mbar_arrive_cluster(bar_tempty_l + 8 * abuf);
-                  else mbar_arrive(bar_tempty + 8 * abuf);
-                }
-                if (threadIdx.x == 128) PCB_TRACE(6, acc_cnt);
-              }
+            uint32_t v[2][CW];
+            auto promote = [&](const uint32_t(&vc)[CW], int c) {
               if constexpr (COL_UNIFORM) {
                 const float2 s2 = make_float2(s_row * s_col, s_row * s_col);
 #pragma unroll
@@ -997,6 +984,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                   acc[a0 + 1] = __ffma2_rn(make_float2(__uint_as_float(vc[4 * q + 2]), __uint_as_float(vc[4 * q + 3])),
                                            sb2, acc[a0 + 1]);
                 }
+              }
+            };
+            tmem_ld32_nowait(taddr, v[0]);
+            tmem_wait_ld();
+            tmem_regs_ready(v[0]);
+#pragma unroll
+            for (int c = 0; c < NCH; ++c) {
+              if (c + 1 < NCH) {
+                tmem_ld32_nowait(taddr + (c + 1) * CW, v[(c + 1) & 1]);
+              } else {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                  if constexpr (PAIR) mbar_arrive_cluster(bar_tempty_l + 8 * abuf);
+                  else mbar_arrive(bar_tempty + 8 * abuf);
+                }
+                if (threadIdx.x == 128) PCB_TRACE(6, acc_cnt);
+              }
+              promote(v[c & 1], c);
+              if (c + 1 < NCH) {
+                tmem_wait_ld();
+                tmem_regs_ready(v[(c + 1) & 1]);
               }
             }
           }
