@@ -724,8 +724,14 @@ CFG4_M, CFG4_K, CFG4_N = 16384, 4096, 14336
 
 def run_cfg4(args, d: Dist) -> dict:
     """Quantize-then-GEMM of X [16384, 4096] (1x128, rows sharded) with the
-    pre-quantized W [4096, 14336] (128x128): the quantize-once path (two
-    launches) and the single fused kernel."""
+    pre-quantized W [4096, 14336] (128x128).
+
+    ``quant_bmm_fused`` takes the quantize-once path here (the 1x128
+    quantizer, then the per-block GEMM: two launches); the one-launch kernel
+    that re-quantizes its activation tile inside every output tile is timed
+    beside it (``per_tile_requant_kernel``), and the quantizer alone
+    (``quantize_x_only_ms``) bounds what any fusion could save: hiding all of
+    the quantization would give ``ideal_fused_ms``."""
     import oracle
     from practice_cuda_b200 import get_quant
     from practice_cuda_b200.fused import quant_bmm_fused
@@ -746,7 +752,7 @@ def run_cfg4(args, d: Dist) -> dict:
     res = {}
     stream = torch.cuda.current_stream(device)
     yw, sw = oracle.per_block_quant(w, block_m=128, block_n=128)
-    for path, fuse in (("quantize_once", False), ("fused", True)):
+    for path, fuse in (("quantize_once", False), ("per_tile_requant_kernel", True)):
         for _ in range(args.warmup):
             quant_bmm_fused(x, qw, out=out, fuse=fuse)
         torch.cuda.synchronize(device)
@@ -773,11 +779,17 @@ def run_cfg4(args, d: Dist) -> dict:
                      "parity": {"ok": d.all_and(q_ok and c_ok), "c_max_rel_err": max(d.max([rel])),
                                 "checked": "first 128-row block of every rank: quantized X bytes + scales "
                                            "bit-exact, C within 1e-2 of the oracle"}}
+    qx_fn = get_quant("b200_per_block_1x128_128x128").fn
+    qx_ms = max(d.max([time_cold(lambda: qx_fn(x, block_m=1, block_n=128), device, 5)]))
     del x, qw, out
     torch.cuda.empty_cache()
     return {"workload": f"cfg4 quantize X 1x128 + per-block GEMM {CFG4_M}x{CFG4_K}x{CFG4_N}, rows sharded "
                         f"x{d.world} ({rows} rows per rank), W pre-quantized 128x128",
-            **res, "gpu_launches_per_step": {"quantize_once": 2, "fused": 1}}
+            "path": "quant_bmm_fused(fuse=None) runs quantize_once at this N (the per-tile re-quantizing "
+                    "kernel is used only for N <= 256)",
+            **res, "quantize_x_only_ms": qx_ms,
+            "ideal_fused_ms": res["quantize_once"]["ms_per_step"] - qx_ms,
+            "gpu_launches_per_step": {"quantize_once": 2, "per_tile_requant_kernel": 1}}
 
 
 # -------------------------------------------------------------------- cfg5 ---

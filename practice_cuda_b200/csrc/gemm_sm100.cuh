@@ -617,6 +617,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Launched with programmatic stream serialization: barrier set-up, TMEM
+  // allocation and tensor-map prefetch overlap the previous kernel's tail;
+  // nothing global is read or written before that kernel has completed.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   PCB_CTA_SPAN(0);
 
   if (p.inject_error && blockIdx.x == 0 && threadIdx.x == 0) report_error(p.inject_error, SITE_GEMM_INJECTED);

@@ -389,17 +389,30 @@ int launch_bmm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& 
     cfg.blockDim = dim3(gemm::kThreads, 1, 1);
     cfg.dynamicSmemBytes = S::ALLOC;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    // The kernel's prologue may overlap the previous kernel (griddepcontrol.wait
+    // precedes every global access).
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, p);
+  } else {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)std::min(p.num_tiles, sm_count), 1, 1);
+    cfg.blockDim = dim3(gemm::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = S::ALLOC;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, p);
-  } else {
-    const int grid = std::min(p.num_tiles, sm_count);
-    kernel<<<grid, gemm::kThreads, S::ALLOC, stream>>>(ta, tb, tc, p);
   }
   return check_launch("bmm_scaled_kernel");
 }

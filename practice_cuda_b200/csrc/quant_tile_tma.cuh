@@ -94,6 +94,10 @@ __global__ void __launch_bounds__(kThreads, CTAS_)
     gemm::prefetch_tmap(&tmap);
   }
   __syncthreads();
+  // A dependent kernel launched with programmatic stream serialization (the
+  // scaled BMM) may start its prologue now; it waits for this grid to finish
+  // before it reads anything.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (t == 0)
     for (int s = 0; s < kTileStages && s < mine; ++s) issue(s, first + s * step);
 
