@@ -112,6 +112,25 @@ def test_bias_activation_out_dtype(out_dtype, activation):
     assert_bmm_close(out, ref, f"{out_dtype} {activation}")
 
 
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", [(2, 300, 384, 264), (1, 260, 256, 520), (3, 384, 128, 136)])
+def test_pair_tma_store_ragged(out_dtype, shape):
+    """CTA-pair tiles whose bf16 / fp16 output rows are 16-byte aligned leave
+    through TMA box stores; rows and columns past M and N (partial 256 x 256
+    tiles, partial 32 x 64 boxes) must be clipped, with bias and GELU applied."""
+    B, M, K, N = shape
+    a = synthetic((B, M, K), outliers=True, seed=M + 1)
+    b = synthetic((B, K, N), std=0.05, seed=N + 2)
+    bias = synthetic((B, M, N), seed=3, dtype=torch.float32)
+    qa, qb, ablk, bblk = _quant_pair("1x128_128x128", a, b)
+    ref = _promoted_ref(qa, qb, ablk, bblk, bias=bias, activation="gelu")
+    out = torch.full((B, M, N), float("nan"), device=DEV, dtype=out_dtype)
+    get_bmm("b200_per_block_1x128_128x128_a_k_b_n").fn(qa, qb, out=out, out_dtype=out_dtype, bias=bias.to(DEV),
+                                                         activation="gelu")
+    assert torch.isfinite(out.float()).all(), "an output element was not written"
+    assert_bmm_close(out, ref, f"pair tma store {out_dtype} {shape}")
+
+
 def test_out_argument_and_k_tail():
     B, M, K, N = 1, 256, 200, 256  # K = 128 + 72: a partial second K group
     a = synthetic((B, M, K), seed=4)
