@@ -53,6 +53,7 @@ static_assert(128 * kLowRegs + 256 * kHighRegs == kThreads * kLaunchRegs, "regis
 constexpr int kNumAcc = 4;        // TMEM accumulator buffers of BN fp32 columns
 constexpr int kScaleWin = 8;      // K groups of scales per shared-memory window
 constexpr int kScaleSlots = 4;    // windows in the shared-memory scale ring
+constexpr int kScaleWinCols = 4;  // K groups per window when B scales vary per column
 constexpr int kScaleThreads = 64; // scale-loader threads (warps 2-3)
 
 // Profiling switches (Params::debug_flags) exist only in builds compiled with
@@ -103,6 +104,10 @@ struct Params {
   long long ssbb, ssbk, ssbn;
   int qbn;
   int col_uniform;  // sb constant over each warpgroup's column half
+  // Per-column B scales only: 16-byte scale loads.  sa_vec 2 = rows
+  // contiguous per K group (qbm == 1); sb_vec = B scales contiguous along N
+  // (qbn == 1).  0 = scalar loads.
+  int sa_vec, sb_vec;
   // output / bias
   void* c;
   long long scb, scm;
@@ -361,7 +366,7 @@ __host__ __device__ constexpr uint32_t make_idesc(int bn, int a_fmt, int b_fmt, 
          ((uint32_t)b_mn << 16) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
-template <int BN, bool PAIR = false>
+template <int BN, bool PAIR = false, bool COLU = true>
 struct Smem {
   // A CTA pair splits the B tile: each CTA stages BN/2 of its N rows.
   static constexpr int B_ROWS = PAIR ? BN / 2 : BN;
@@ -372,10 +377,12 @@ struct Smem {
   static constexpr int EPI_COLS = BN / 2;
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
-  static constexpr int OFF_COLSCALE = OFF_B + STAGES * B_BYTES;           // 8 warps x EPI_COLS floats
-  // Scale ring slot: row scales [kScaleWin][BM], then uniform B scales [kScaleWin][2].
-  static constexpr int SC_SLOT = kScaleWin * (BM + 2);
-  static constexpr int OFF_SCALE = OFF_COLSCALE + 8 * EPI_COLS * 4;
+  static constexpr int OFF_COLSCALE = OFF_B + STAGES * B_BYTES;           // (unused)
+  // Scale ring slot of SW K groups: row scales [SW][BM], then the B scales:
+  // uniform ones [SW][2] (one per 128-column block) or per column [SW][BN].
+  static constexpr int SW = COLU ? kScaleWin : kScaleWinCols;
+  static constexpr int SC_SLOT = SW * (BM + (COLU ? 2 : BN));
+  static constexpr int OFF_SCALE = OFF_COLSCALE + (COLU ? 8 * EPI_COLS * 4 : 0);
   static constexpr int OFF_BAR = OFF_SCALE + kScaleSlots * SC_SLOT * 4;
   static constexpr int NUM_BARS = 2 * STAGES + 2 * kNumAcc + 2 * kScaleSlots;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;                  // tmem addr, abort flag
@@ -550,13 +557,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     bmm_scaled_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                       const __grid_constant__ CUtensorMap tmap_c, const Params p) {
   static_assert(!PAIR || BN == 256, "the CTA pair runs 256x256 tiles");
-  using S = Smem<BN, PAIR>;
+  using S = Smem<BN, PAIR, COL_UNIFORM>;
   constexpr int STAGES = S::STAGES;
   constexpr int EPI_COLS = S::EPI_COLS;
   constexpr int NACC = (BN == 256) ? 2 : kNumAcc;  // TMEM accumulator buffers of BN columns
   constexpr uint32_t TMEM_COLS = NACC * BN;
   static_assert(NACC * BN <= 512, "TMEM holds 512 fp32 columns");
-  constexpr int W = kScaleWin;
+  constexpr int W = S::SW;
   const uint32_t IDESC = make_idesc(BN, p.a_fmt, p.b_fmt, A_MN ? 1 : 0, B_MN ? 1 : 0, PAIR ? 2 * BM : BM);
   // Bytes that land on the (leader's) full barrier per stage.
   constexpr uint32_t STAGE_TX = (PAIR ? 2 : 1) * (S::A_BYTES + S::B_BYTES);
@@ -810,11 +817,65 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         float* dst = sring + slot * S::SC_SLOT;
+        // Per-column B scales: one pass of 16-byte loads where the layouts
+        // allow (rounds of scalar loads per window were slower than the
+        // epilogue consumes windows).
+        const bool vec_rows = !COL_UNIFORM && p.sa_vec == 2 && row0 + BM <= p.m;
+        if constexpr (!COL_UNIFORM) {
+          if (vec_rows) {
+            // Rows contiguous per K group: BM / 4 float4 per group.
+            constexpr int U = W * (BM / 4) / kScaleThreads;
+            float4 v[U];
+#pragma unroll
+            for (int i = 0; i < U; ++i) {
+              const int u = t + i * kScaleThreads, gw = u / (BM / 4), rq = u % (BM / 4);
+              v[i] = g0 + gw < p.num_groups
+                         ? __ldg(reinterpret_cast<const float4*>(sa_b + row0 + 4 * rq + (long long)(g0 + gw) * p.ssak))
+                         : make_float4(1.f, 1.f, 1.f, 1.f);
+            }
+#pragma unroll
+            for (int i = 0; i < U; ++i) {
+              const int u = t + i * kScaleThreads, gw = u / (BM / 4), rq = u % (BM / 4);
+              *reinterpret_cast<float4*>(dst + gw * BM + 4 * rq) = v[i];
+            }
+          }
+          // Per-column B scales of the tile's BN columns, [gw][col].
+          if (p.sb_vec && g0 + W <= p.num_groups && nb * BN + BN <= p.n) {
+            constexpr int U = W * (BN / 4) / kScaleThreads;
+            float4 v[U];
+#pragma unroll
+            for (int i = 0; i < U; ++i) {
+              const int u = t + i * kScaleThreads, gw = u / (BN / 4), cq = u % (BN / 4);
+              v[i] = __ldg(reinterpret_cast<const float4*>(sb_b + (long long)(g0 + gw) * p.ssbk + nb * BN + 4 * cq));
+            }
+#pragma unroll
+            for (int i = 0; i < U; ++i) {
+              const int u = t + i * kScaleThreads, gw = u / (BN / 4), cq = u % (BN / 4);
+              *reinterpret_cast<float4*>(dst + BM * W + gw * BN + 4 * cq) = v[i];
+            }
+          } else {
+            constexpr int PER_C = W * BN / kScaleThreads, PC = 8;
+#pragma unroll 1
+            for (int i0 = 0; i0 < PER_C; i0 += PC) {
+              float v[PC];
+#pragma unroll
+              for (int i = 0; i < PC; ++i) {
+                const int e = t + (i0 + i) * kScaleThreads;
+                const int g = g0 + e / BN, col = nb * BN + e % BN;
+                v[i] = (sb_b && col < p.n && g < p.num_groups)
+                           ? __ldg(sb_b + (long long)g * p.ssbk + (long long)(col / p.qbn) * p.ssbn)
+                           : 1.f;
+              }
+#pragma unroll
+              for (int i = 0; i < PC; ++i) dst[BM * W + t + (i0 + i) * kScaleThreads] = v[i];
+            }
+          }
+        }
         // Element e = r + BM * gw (rows fastest: conflict-free shared stores);
-        // thread t takes e = t + 64 i, in passes of 4 loads in flight.
+        // thread t takes e = t + 64 i, in passes of 8 loads in flight.
         constexpr int PER_T = BM * W / kScaleThreads, PASS = 8;
 #pragma unroll 1
-        for (int i0 = 0; i0 < PER_T; i0 += PASS) {
+        for (int i0 = vec_rows ? PER_T : 0; i0 < PER_T; i0 += PASS) {
           float v[PASS];
 #pragma unroll
           for (int i = 0; i < PASS; ++i) {
@@ -845,8 +906,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;           // TMEM lane quarter
     const int half = ew >> 2;               // column half
     const int row_in_tile = quarter * 32 + lane;
-    float* colscale = reinterpret_cast<float*>(smem + S::OFF_COLSCALE) + ew * EPI_COLS;
-    const uint32_t colscale_s = smem_u32(colscale);
     uint32_t acc_cnt = 0;
     uint32_t wc = 0;  // scale windows consumed
     bool ok = true;
@@ -859,25 +918,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int nb = rem - mb * p.n_blocks;
       const int row = mb * TILE_M + (int)rank * BM + row_in_tile;
       const int col0 = nb * BN + half * EPI_COLS;
-      const float* sb_b = p.sb ? p.sb + (long long)b * p.ssbb : nullptr;
 
       float2 acc[EPI_COLS / 2];
 #pragma unroll
       for (int i = 0; i < EPI_COLS / 2; ++i) acc[i] = make_float2(0.f, 0.f);
 
-      // Per-column scales (non-uniform B scales): lane l holds columns
-      // col0 + 32 q + l of the next K group.
-      float cnx[EPI_COLS / 32];
-      auto load_cols = [&](int g) {
-#pragma unroll
-        for (int q = 0; q < EPI_COLS / 32; ++q) {
-          const int c = col0 + q * 32 + lane;
-          cnx[q] = (sb_b && c < p.n && g < p.num_groups)
-                       ? __ldg(sb_b + (long long)g * p.ssbk + (long long)(c / p.qbn) * p.ssbn)
-                       : 1.f;
-        }
-      };
-      if constexpr (!COL_UNIFORM) load_cols(0);
       // Pair tiles with uniform B scales: two groups per loop iteration (the
       // loop-back of a single group costs ~200 cycles of the ~750 a group
       // takes on the epilogue's critical path).  The other variants keep one
@@ -897,20 +942,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float* ws = sring + slot * S::SC_SLOT;
           const float s_row = ws[gw * BM + row_in_tile];
           const float s_col = COL_UNIFORM ? ws[BM * W + gw * 2 + half] : 1.f;
-          if (gw == W - 1 || g + 1 == p.num_groups) {
+          // Per-column B scales of this group and this warp's columns (read
+          // from the ring during the promotion, so the slot is handed back
+          // after it; uniform scales were read above and free it now).
+          const float* colscale = ws + BM * W + gw * BN + half * EPI_COLS;
+          const uint32_t colscale_s = smem_u32(colscale);
+          const bool win_end = gw == W - 1 || g + 1 == p.num_groups;
+          if (COL_UNIFORM && win_end) {
             // This warp has read the window's scales.
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_sempty + 8 * slot);
             ++wc;
-          }
-          if constexpr (!COL_UNIFORM) {
-            // Publish this group's column scales (loaded one group ahead) to
-            // the warp's shared slice, then start loading the next group's.
-            __syncwarp();
-#pragma unroll
-            for (int q = 0; q < EPI_COLS / 32; ++q) colscale[q * 32 + lane] = cnx[q];
-            __syncwarp();
-            load_cols(g + 1);
           }
           if (threadIdx.x == 128) PCB_TRACE(4, acc_cnt);
           if (!(PAIR ? mbar_spin_bounded_warp(bar_tfull + 8 * abuf, aphase, abort_flag, SITE_GEMM_EPILOGUE)
@@ -925,6 +967,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) {
               if constexpr (PAIR) mbar_arrive_cluster(bar_tempty_l + 8 * abuf);
               else mbar_arrive(bar_tempty + 8 * abuf);
+            }
+            if (!COL_UNIFORM && win_end) {
+              __syncwarp();
+              if (lane == 0) mbar_arrive(bar_sempty + 8 * slot);
+              ++wc;
             }
             ++acc_cnt;
             continue;
@@ -1012,6 +1059,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_regs_ready(v[(c + 1) & 1]);
               }
             }
+          }
+          if (!COL_UNIFORM && win_end) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_sempty + 8 * slot);
+            ++wc;
           }
           if (threadIdx.x == 128) PCB_TRACE(7, acc_cnt);
           ++acc_cnt;

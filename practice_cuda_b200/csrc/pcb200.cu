@@ -366,7 +366,7 @@ int launch_fused(const CUtensorMap& tx, const CUtensorMap& tb, const gemm::Param
 template <int BN, bool A_MN, bool B_MN, bool COLU, bool PAIR>
 int launch_bmm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const gemm::Params& p,
                int sm_count, cudaStream_t stream) {
-  using S = gemm::Smem<BN, PAIR>;
+  using S = gemm::Smem<BN, PAIR, COLU>;
   auto kernel = gemm::bmm_scaled_kernel<BN, A_MN, B_MN, COLU, PAIR>;
   if constexpr (BN == 256) {
     // This instantiation re-splits its registers with setmaxnreg; the split
@@ -973,6 +973,10 @@ static int bmm_entry(const void* a, int64_t sab, int64_t sam, int64_t sak, const
   p.ssbn = ssbn;
   p.qbn = (int)std::min<int64_t>(qbn, INT32_MAX);
   p.col_uniform = (!scale_b || ssbn == 0 || qbn % epi_cols == 0 || qbn >= n) ? 1 : 0;
+  p.sa_vec = (scale_a && aligned(scale_a, 16) && (batch == 1 || ssab % 4 == 0) && qbm == 1 && ssam == 1 &&
+              ssak % 4 == 0) ? 2 : 0;
+  p.sb_vec = (scale_b && aligned(scale_b, 16) && (batch == 1 || ssbb % 4 == 0) && qbn == 1 && ssbn == 1 &&
+              ssbk % 4 == 0) ? 1 : 0;
   p.c = c;
   p.scb = scb;
   p.scm = scm;
