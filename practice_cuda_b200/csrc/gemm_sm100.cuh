@@ -498,7 +498,7 @@ __device__ __forceinline__ void store_row(const Params& p, float* accf, int b, i
 }
 
 // Bias, activation and a TMA store of one warp's 32 rows x EPI_COLS columns
-// of bf16 / fp16 C, 64 columns at a time: every lane writes its row's 128
+// of bf16 / fp16 C, 64 columns at a time (fp32 C: 32 at a time): every lane writes its row's 128
 // bytes into the warp's 4 KB staging buffer (128-byte swizzle: conflict-free)
 // and lane 0 stores the 32 x 64 box.  Whole 128-byte row segments keep the
 // store engine's request count low (per-thread 16-byte row stores cost ~9000
@@ -524,6 +524,25 @@ __device__ __forceinline__ void store_rows_tma(const Params& p, const CUtensorMa
   }
   const bool bf16 = p.c_dtype == PCB_DTYPE_BF16;
   const uint32_t swz = (uint32_t)(lane & 7);
+  if (p.c_dtype == PCB_DTYPE_F32) {
+    // fp32: 32-column boxes (128-byte rows), EPI_COLS / 32 per warp.
+#pragma unroll
+    for (int q = 0; q < EPI_COLS / 32; ++q) {
+      if (lane == 0) bulk_wait_read<0>();
+      __syncwarp();
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const float* f = accf + 32 * q + 4 * c;
+        const uint32_t dst = stg + (uint32_t)lane * 128u + (((uint32_t)c ^ swz) << 4);
+        asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "f"(f[0]), "f"(f[1]), "f"(f[2]), "f"(f[3])
+                     : "memory");
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && warp_row0 < p.m && col0 + 32 * q < p.n) tma_store_3d(tmap_c, stg, col0 + 32 * q, warp_row0, b);
+    }
+    return;
+  }
 #pragma unroll
   for (int q = 0; q < EPI_COLS / 64; ++q) {
     if (lane == 0) bulk_wait_read<0>();

@@ -319,19 +319,21 @@ bool make_map_x16(CUtensorMap* map, const void* base, int dt, uint64_t inner, ui
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// 3-D map of a bf16 / fp16 output C (n, m, batch) for TMA stores of 64-column
-// x 32-row boxes in the 128-byte swizzle (the pair epilogue's staging layout).
-bool make_map_c16(CUtensorMap* map, void* base, int dt, uint64_t n, uint64_t m, uint64_t batch,
+// 3-D map of a bf16 / fp16 / fp32 output C (n, m, batch) for TMA stores of
+// 32-row boxes with 128-byte rows (64 or 32 columns) in the 128-byte swizzle
+// (the pair epilogue's staging layout).
+bool make_map_c(CUtensorMap* map, void* base, int dt, uint64_t n, uint64_t m, uint64_t batch,
                   uint64_t row_stride_bytes, uint64_t batch_stride_bytes) {
   auto fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[3] = {n, m, batch};
   if (batch <= 1) batch_stride_bytes = std::max<uint64_t>(16, ((m * row_stride_bytes + 15) / 16) * 16);
   cuuint64_t strides[2] = {row_stride_bytes, batch_stride_bytes};
-  cuuint32_t box[3] = {64, 32, 1};
+  cuuint32_t box[3] = {dt == PCB_DTYPE_F32 ? 32u : 64u, 32, 1};  // 128-byte box rows
   cuuint32_t estr[3] = {1, 1, 1};
-  const CUtensorMapDataType t =
-      dt == PCB_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUtensorMapDataType t = dt == PCB_DTYPE_BF16  ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                : dt == PCB_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   return fn(map, t, 3, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -1023,9 +1025,9 @@ static int bmm_entry(const void* a, int64_t sab, int64_t sam, int64_t sak, const
   // epilogue, and with it the MMA, for thousands of cycles per tile).
   CUtensorMap tc;
   std::memset(&tc, 0, sizeof(tc));
-  if (pair && (c_dtype == PCB_DTYPE_BF16 || c_dtype == PCB_DTYPE_F16) && p.c_vec)
-    p.c_tma = make_map_c16(&tc, c, c_dtype, (uint64_t)n, (uint64_t)m, (uint64_t)batch, (uint64_t)scm * 2,
-                           (uint64_t)scb * 2) ? 1 : 0;
+  if (pair && (c_dtype == PCB_DTYPE_BF16 || c_dtype == PCB_DTYPE_F16 || c_dtype == PCB_DTYPE_F32) && p.c_vec)
+    p.c_tma = make_map_c(&tc, c, c_dtype, (uint64_t)n, (uint64_t)m, (uint64_t)batch, (uint64_t)(scm * ces),
+                           (uint64_t)(scb * ces)) ? 1 : 0;
   if (pair) return dispatch_bmm_layout<256, true>(a_mn, b_mn, ta, tb, tc, p, di.sm_count, s);
   if (bn == 256) return dispatch_bmm_layout<256, false>(a_mn, b_mn, ta, tb, tc, p, di.sm_count, s);
   return dispatch_bmm_layout<128, false>(a_mn, b_mn, ta, tb, tc, p, di.sm_count, s);

@@ -112,10 +112,10 @@ def test_bias_activation_out_dtype(out_dtype, activation):
     assert_bmm_close(out, ref, f"{out_dtype} {activation}")
 
 
-@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("shape", [(2, 300, 384, 264), (1, 260, 256, 520), (3, 384, 128, 136)])
 def test_pair_tma_store_ragged(out_dtype, shape):
-    """CTA-pair tiles whose bf16 / fp16 output rows are 16-byte aligned leave
+    """CTA-pair tiles whose bf16 / fp16 / fp32 output rows are 16-byte aligned leave
     through TMA box stores; rows and columns past M and N (partial 256 x 256
     tiles, partial 32 x 64 boxes) must be clipped, with bias and GELU applied."""
     B, M, K, N = shape
@@ -269,3 +269,30 @@ def test_per_block_pair_and_single(layout, m):
     qa2, qb2 = _operands_for_layout(qa, qb, layout)
     out = get_bmm(f"b200_per_block_1x128_128x128_{layout}").fn(qa2, qb2)
     assert_bmm_close(out, ref, f"per-block M={m} {layout}")
+
+
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("shape", [(384, 512, 512), (300, 640, 520), (512, 384, 1024)])
+def test_per_column_scales_wgrad_layout(out_dtype, shape):
+    """The weight-gradient GEMM of the FP8 training linear: A M-major with
+    row scales contiguous along M per K group, B N-major with per-column
+    scales contiguous along N per K group (16-byte scale loads on full tiles,
+    scalar loads on partial ones), fp32 or bf16 output."""
+    from practice_cuda_b200.fp8_linear import _gemm
+
+    M, K, N = shape
+    g = torch.Generator().manual_seed(M + N)
+    a = (torch.randn(M, K, generator=g) * 0.2).to(torch.float8_e4m3fn)
+    b = (torch.randn(K, N, generator=g) * 0.2).to(torch.float8_e4m3fn)
+    sa_t = torch.rand(K // 128 + (K % 128 > 0), M, generator=g) + 0.5   # [kg, m]
+    sb = torch.rand(K // 128 + (K % 128 > 0), N, generator=g) + 0.5     # [kg, n]
+    a_dev = a.to(DEV).t().contiguous().t()                             # M-major
+    sa_dev, sb_dev = sa_t.to(DEV), sb.to(DEV)
+    out = _gemm(a_dev, sa_dev, (sa_dev.stride(1), sa_dev.stride(0)), 1, b.to(DEV), sb_dev, tuple(sb_dev.stride()), 1,
+                out_dtype)
+    ref = torch.zeros(M, N)
+    for kg in range(sa_t.shape[0]):
+        ks = slice(128 * kg, min(K, 128 * kg + 128))
+        ref += (a[:, ks].float() @ b[ks].float()) * sa_t[kg][:, None] * sb[kg][None, :]
+    assert out.dtype == out_dtype
+    assert_bmm_close(out, ref, f"wgrad layout {out_dtype} {shape}")
